@@ -1,0 +1,241 @@
+#!/usr/bin/env python
+"""Benchmark: kernel-matvec TFLOP/s at n=1M, d=16, t=16 (RBF-ARD) on 1..8 B200.
+
+One step = one matrix-free K(X,X)·V + sigma^2 V with t=16 right-hand sides over
+the seeded config-3 inputs (X ~ N(0, I)^{1e6 x 16}, l ~ U[0.5, 3]^16), inputs
+resident in HBM. With N GPUs the training rows are sharded (each rank owns
+n/N rows of the output; X and V are replicated) and every step ends with the
+NCCL all-gather of the output row blocks, as one CG iteration needs.
+
+Prints one JSON line (rank 0). `--impl reference` times the reference's CPU
+route (NumPy kernel evaluator + BLAS, restated in oracle/cpu_baseline.py) on
+the host cores instead.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+from pathlib import Path
+
+import numpy as np
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+METRIC = "kernel-matvec TFLOP/s & fit s/iter at n=1M,d=16,t=16"
+UNIT = "TFLOP/s"
+F_PER_PAIR_RBF = lambda d, t: 3 * d + 3 + 2 * t  # algorithmic flops per kernel entry
+
+
+def parse():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=5)
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--n", type=int, default=1_000_000)
+    ap.add_argument("--d", type=int, default=16)
+    ap.add_argument("--t", type=int, default=16)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-seconds", type=float, default=12.0)
+    return ap.parse_args()
+
+
+class ClockSampler:
+    """nvidia-smi clocks / throttle reasons sampled every 200 ms."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.file = tempfile.NamedTemporaryFile("w+", suffix=".csv", delete=False)
+        self.proc = None
+        self.gpu = gpu_index
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200", "-i", str(self.gpu)], stdout=self.file, stderr=subprocess.DEVNULL)
+        except FileNotFoundError:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        self.proc.wait()
+        self.file.flush()
+        rows = [r.split(",") for r in Path(self.file.name).read_text().strip().splitlines() if r]
+        os.unlink(self.file.name)
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for r in rows:
+            r = [x.strip() for x in r]
+            try:
+                sm.append(float(r[1]))
+                smax.append(float(r[2]))
+            except (ValueError, IndexError):
+                continue
+            for nm, v in zip(names, r[5:9]):
+                if v.lower() == "active":
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None,
+                "sm_max_mhz": max(smax) if smax else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def run_reference(args, rank: int, world: int) -> None:
+    """CPU arm: the reference's NumPy route on the host cores (rank 0 only)."""
+    if rank != 0:
+        return
+    from mojogp_b200 import synthetic
+    from oracle import cpu_baseline
+    X, _, ell = synthetic.config3(n=args.n, d=args.d)
+    V = synthetic.probes_v(args.n, args.t, seed=1)
+    threads = os.cpu_count() or 1
+    per_step = []
+    for it in range(args.warmup + args.steps):
+        r = cpu_baseline.time_matvec_sample(X, V, ell, 1.0, target_s=max(2.0, 30.0 / max(args.steps + args.warmup, 1)),
+                                            threads=threads, max_rows=2048)
+        if it >= args.warmup:
+            per_step.append(r)
+    F = F_PER_PAIR_RBF(args.d, args.t)
+    tflops = [r["pairs_per_s"] * F / 1e12 for r in per_step]
+    value = statistics.median(tflops)
+    rows = per_step[-1]["rows"]
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": 1e3 * statistics.median(r["seconds"] for r in per_step),
+        "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f64",
+        "data": "synthetic (config 3 recipe, seed 3)",
+        "config": {"workload": "config3 K(X,X)V RBF-ARD", "n": args.n, "d": args.d, "t": args.t,
+                   "sample": f"{rows} rows x {args.n} columns per step"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
+                         "sample": f"{rows} output rows x all {args.n} columns, float64 NumPy "
+                                   "evaluator (kernel.py:804-923 route) + BLAS"},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if args.impl == "reference":
+        run_reference(args, rank, world)
+        return
+
+    from mojogp_b200 import _lib, synthetic
+    from mojogp_b200.kernel import RBF, make_ard_kernel
+    from mojogp_b200.provider import DeviceBuffer, Provider
+    import ctypes as C
+
+    comm = None
+    if world > 1:
+        from mojogp_b200.distributed import Communicator
+        comm = Communicator.from_env(device=local)
+
+    n, d, t = args.n, args.d, args.t
+    X, _, ell = synthetic.config3(n=n, d=d)
+    params = np.concatenate([ell, [1.0]]).astype(np.float32)
+    kern = make_ard_kernel(RBF(ard=True), d)
+    prov = Provider(X, kern, params, noise=0.0025, device=local)
+    V = synthetic.probes_v(n, t, seed=1)
+    Vc = np.ascontiguousarray(V.T)
+    vd = DeviceBuffer.from_host(Vc, local)
+    r0, r1 = (rank * n) // world, ((rank + 1) * n) // world
+    od = DeviceBuffer((t, n), local)
+
+    F = F_PER_PAIR_RBF(d, t)
+    flops_total = float(n) * n * F  # whole job per step
+    flops_local = float(r1 - r0) * n * F
+
+    # Measured FP32 roofline denominator.
+    peak_tf, peak_ms = C.c_double(), C.c_double()
+    _lib.call("gpb_measure_fp32_peak", local, C.byref(peak_tf), C.byref(peak_ms))
+
+    sampler = ClockSampler(local)
+    if comm:
+        comm.barrier()
+    sampler.start()
+    steps, warm = args.steps, args.warmup
+    step_ms = np.zeros(steps)
+    kern_ms = np.zeros(steps)
+    launches = np.zeros(steps, dtype=np.int64)
+    if comm is None:
+        _lib.call("gpb_benchmark_forward", prov.h, vd.cptr, od.cptr, t, warm, steps, 1,
+                  C.c_void_p(step_ms.ctypes.data), C.c_void_p(kern_ms.ctypes.data),
+                  C.c_void_p(launches.ctypes.data))
+    else:
+        res = comm.benchmark_sharded_forward(prov, vd, od, t, warm, steps, r0, r1)
+        step_ms[:], kern_ms[:], launches[:] = res
+    clocks = sampler.stop()
+
+    total_ms = float(step_ms.sum())
+    if comm:
+        total_ms = comm.allreduce_max(total_ms)
+        kmean = comm.allreduce_max(float(kern_ms.mean()))
+    else:
+        kmean = float(kern_ms.mean())
+    value = flops_total * steps / (total_ms * 1e-3) / 1e12
+
+    # End to end through the C ABI with host buffers (H2D V, matvec, D2H out).
+    e2e_tf = None
+    if comm is None:
+        out_h = np.empty_like(Vc)
+        t0 = time.perf_counter()
+        for _ in range(max(1, min(steps, 3))):
+            _lib.call("gpb_forward_matvec_host", prov.h, C.c_void_p(out_h.ctypes.data),
+                      C.c_void_p(Vc.ctypes.data), t)
+        e2e_s = (time.perf_counter() - t0) / max(1, min(steps, 3))
+        e2e_tf = flops_total / e2e_s / 1e12
+    else:
+        e2e_tf = comm.e2e_sharded(prov, Vc, t, r0, r1, flops_total)
+
+    achieved = flops_local / (kmean * 1e-3) / 1e12
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": steps,
+        "warmup": warm, "ms_per_step": total_ms / steps, "higher_is_better": True,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (config 3 recipe: X~N(0,I), l~U[0.5,3], seed 3)",
+        "config": {"workload": "config3 K(X,X)V RBF-ARD matrix-free, t=16", "n": n, "d": d,
+                   "t": t, "parallelism": f"row-shard x{world}",
+                   "l2": "256 MB flush before every step; packed column tiles 128 MB"},
+        "gpu_launches": int(launches.sum()),
+        "e2e": {"value": e2e_tf, "unit": UNIT, "h2d_bytes_per_step": int(Vc.nbytes),
+                "d2h_bytes_per_step": int(Vc.nbytes)},
+        "roofline": {"bound": "fp32", "achieved": achieved, "peak": peak_tf.value,
+                     "unit": "TFLOP/s", "frac": achieved / peak_tf.value, "traffic": None,
+                     "peak_source": "measured FFMA probe (gpb_measure_fp32_peak) on this GPU",
+                     "nominal_peak": 148 * 128 * 2 * 1.965e9 / 1e12,
+                     "flops_per_pair": F},
+        "clocks": clocks,
+    }
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        from oracle import cpu_baseline
+        Xs = X
+        r = cpu_baseline.time_matvec_sample(Xs, V, ell, 1.0, target_s=args.cpu_seconds,
+                                            max_rows=1024)
+        line["cpu_baseline"] = {
+            "value": r["pairs_per_s"] * F / 1e12, "unit": UNIT, "cores": r["threads"],
+            "kind": "port",
+            "sample": f"{r['rows']} output rows x all {n} columns (float64 NumPy evaluator + BLAS)"}
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if comm:
+        comm.close()
+
+
+if __name__ == "__main__":
+    main()

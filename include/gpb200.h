@@ -1,0 +1,178 @@
+/*
+ * gpb200 — B200-native exact Gaussian-process hot path, C ABI.
+ *
+ * This is the drop-in boundary for MojoGP's JIT kernel-module / engine slot.
+ * The reference splits the hot path into a per-kernel "provider" module whose
+ * init_provider() returns a dict of raw function pointers
+ * (mojogp/codegen_engine/emit/fn_ptr_module.py:998-1169) and an engine module
+ * that consumes them (mojogp/kernels/jit/jit_engine_bindings.mojo:123-1234).
+ * Each entry point below names the reference function-pointer or binding it
+ * replaces. Conventions:
+ *   - every function returns an int status (GPB_OK == 0, negative on error);
+ *     gpb_last_error() returns the thread's last message;
+ *   - "_dev" pointers are device pointers on the provider's device, "_host"
+ *     pointers are host memory;
+ *   - column blocks are column-major [ncols][n]: element (i, c) at c*n + i,
+ *     matching the reference layout (gpu_kernel.py:225-228, 257-258);
+ *   - X is row-major [n][d] float32;
+ *   - calls on one provider are ordered on that provider's CUDA stream; call
+ *     gpb_provider_synchronize() before reading results on the host.
+ */
+#ifndef GPB200_H
+#define GPB200_H
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ---------------------------------------------------------------- status */
+#define GPB_OK 0
+#define GPB_ERR_INVALID (-1)   /* bad argument (shape, null pointer, range) */
+#define GPB_ERR_CUDA (-2)      /* CUDA runtime error */
+#define GPB_ERR_NOMEM (-3)     /* device allocation failed */
+#define GPB_ERR_UNSUPPORTED (-4)
+#define GPB_ERR_DEVICE (-5)    /* a kernel reported a device-side error word */
+#define GPB_ERR_NCCL (-6)
+#define GPB_ERR_NUMERIC (-7)
+
+/* ----------------------------------------------------------- kernel spec
+ * A kernel tree is passed as a flat int32 program in post-order, replacing
+ * the reference's SymPy -> Mojo codegen of the same tree
+ * (mojogp/codegen_engine/expressions.py:77-650):
+ *   word 0: GPB_SPEC_VERSION
+ *   word 1: number of kernel parameters P (engine layout, see below)
+ *   word 2: number of nodes
+ *   then per node:
+ *     leaf : GPB_NODE_LEAF, type, ard, param_offset, ndims, dims[ndims]
+ *     sum  : GPB_NODE_SUM
+ *     prod : GPB_NODE_PRODUCT
+ *     scale: GPB_NODE_SCALE, param_index
+ * Parameter layout per leaf follows mojogp/kernel.py:324-460
+ * (get_param_names): ARD stationary [l_0..l_{k-1}, (period|alpha), os],
+ * isotropic [ls, (period|alpha), os], linear [variance | var_0..var_{k-1}, os],
+ * polynomial [degree, offset, os] (isotropic; degree is a fixed integer).
+ * A scale node's parameter follows its child's parameters (kernel.py:553-556).
+ */
+#define GPB_SPEC_VERSION 1
+#define GPB_NODE_LEAF 1
+#define GPB_NODE_SUM 2
+#define GPB_NODE_PRODUCT 3
+#define GPB_NODE_SCALE 4
+
+#define GPB_KERNEL_RBF 0
+#define GPB_KERNEL_MATERN12 1
+#define GPB_KERNEL_MATERN32 2
+#define GPB_KERNEL_MATERN52 3
+#define GPB_KERNEL_RQ 4
+#define GPB_KERNEL_PERIODIC 5
+#define GPB_KERNEL_LINEAR 6
+#define GPB_KERNEL_POLYNOMIAL 7
+
+#define GPB_MAX_LEAVES 8
+#define GPB_MAX_NODES 16
+#define GPB_MAX_PARAMS 96
+#define GPB_MAX_DIM 64
+
+/* noise modes (reference fn_ptr_module.py:297-322, modes 0 and 1) */
+#define GPB_NOISE_SCALAR 0
+#define GPB_NOISE_FIXED_VECTOR 1
+
+typedef struct gpb_provider gpb_provider;
+
+/* ---------------------------------------------------------------- library */
+const char* gpb_version(void);
+/* Copies the calling thread's last error message into buf (NUL-terminated). */
+int gpb_last_error(char* buf, int64_t buf_len);
+int gpb_device_count(int32_t* count_out);
+
+/* Plain device-memory helpers so a NumPy host (no torch) can own device
+ * buffers for the provider calls. */
+int gpb_device_alloc(int32_t device, int64_t bytes, void** ptr_out);
+int gpb_device_free(int32_t device, void* ptr);
+int gpb_memcpy_h2d(int32_t device, void* dst_dev, const void* src_host, int64_t bytes);
+int gpb_memcpy_d2h(int32_t device, void* dst_host, const void* src_dev, int64_t bytes);
+int gpb_memset_d(int32_t device, void* dst_dev, int32_t value, int64_t bytes);
+
+/* ---------------------------------------------------------------- provider
+ * Replaces init_provider() (fn_ptr_module.py:998-1115): copies X to the
+ * device and keeps params/noise. noise_vec_host may be NULL (scalar noise);
+ * otherwise it holds n fixed per-row noise variances (noise mode 1).
+ */
+int gpb_provider_create(const float* X_host, int64_t n, int32_t d, const int32_t* spec,
+                        int32_t spec_len, const float* params_host, int32_t num_params,
+                        float noise, const float* noise_vec_host, int32_t device,
+                        gpb_provider** out);
+/* Replaces destroy_provider() (fn_ptr_module.py:1183-1196). */
+int gpb_provider_destroy(gpb_provider* p);
+int gpb_provider_synchronize(gpb_provider* p);
+/* Replaces impl_update_params (fn_ptr_module.py:651-664): host params, P floats. */
+int gpb_update_params(gpb_provider* p, const float* params_host, int32_t num_params);
+/* Replaces update_noise / get_noise / get_noise_mode. */
+int gpb_update_noise(gpb_provider* p, float noise);
+int gpb_get_noise(gpb_provider* p, float* noise_out);
+int gpb_get_noise_mode(gpb_provider* p, int32_t* mode_out);
+int gpb_get_num_params(gpb_provider* p, int32_t* num_out);
+int gpb_get_params(gpb_provider* p, float* params_host, int32_t num_params);
+/* Replaces get_diagonal_value (k(x,x) for a stationary kernel). */
+int gpb_get_diagonal_value(gpb_provider* p, float* value_out);
+/* Device pointer of the provider's X [n][d] (x_ptr in the provider dict). */
+int gpb_get_x_ptr(gpb_provider* p, const float** x_dev_out);
+
+/* Replaces impl_forward_matvec (fn_ptr_module.py:391-490):
+ * out = K(X,X) V + sigma^2 V (scalar noise) or + diag(noise_vec) V. */
+int gpb_forward_matvec(gpb_provider* p, float* out_dev, const float* v_dev, int64_t ncols);
+/* Same, restricted to output rows [row_begin, row_end) (row-sharded matvec):
+ * out has (row_end-row_begin) rows per column, v has all n rows. */
+int gpb_forward_matvec_rows(gpb_provider* p, float* out_dev, const float* v_dev, int64_t ncols,
+                            int64_t row_begin, int64_t row_end);
+/* Host-buffer variant: copies V in, runs the matvec, copies out back. */
+int gpb_forward_matvec_host(gpb_provider* p, float* out_host, const float* v_host,
+                            int64_t ncols);
+/* Replaces impl_cross_matvec (fn_ptr_module.py:576-616): out = K(X*, X) V,
+ * xtest_dev row-major [n_test][d], out [ncols][n_test]. No noise term. */
+int gpb_cross_matvec(gpb_provider* p, float* out_dev, const float* xtest_dev, const float* v_dev,
+                     int64_t n_test, int64_t ncols);
+/* Replaces impl_extract_diagonal / impl_extract_diagonal_test: k(x_i, x_i). */
+int gpb_extract_diagonal(gpb_provider* p, float* diag_dev);
+int gpb_extract_diagonal_test(gpb_provider* p, float* diag_dev, const float* xtest_dev,
+                              int64_t n_test);
+/* Kernel row K(X, x_piv) for one training index (no noise). */
+int gpb_kernel_column(gpb_provider* p, float* out_dev, int64_t pivot);
+
+/* Replaces impl_gradient_matvec (fn_ptr_module.py:511-540 single param) and
+ * impl_fused_gradient_matvec: out[p][c][i] = sum_j dK_ij/dtheta_p V[j,c]
+ * (all P params, layout [P][ncols][n]) — constrained-parameter derivatives. */
+int gpb_gradient_matvec(gpb_provider* p, float* out_dev, const float* v_dev, int64_t ncols,
+                        int32_t param_index);
+int gpb_fused_gradient_matvec(gpb_provider* p, float* out_dev, const float* v_dev,
+                              int64_t ncols);
+/* Fused bilinear gradient reduction (no [P][t][n] intermediate). With a and b
+ * column-major [ncols][n]:
+ *   data_out[p]  = sum_ij a[0,i] dK_ij/dtheta_p b[0,j]
+ *   trace_out[p] = sum_{c>=1} sum_ij a[c,i] dK_ij/dtheta_p b[c,j]
+ * These are exactly the dot products the reference forms after its two fused
+ * gradient matvecs (combined_inv_quad_logdet.mojo:740-785). Outputs are host
+ * arrays of P floats; the call synchronizes. */
+int gpb_gradient_bilinear(gpb_provider* p, const float* a_dev, const float* b_dev, int64_t ncols,
+                          double* data_out, double* trace_out);
+
+/* Replaces benchmark_provider_ops (jit_engine_bindings.mojo:439-567) for the
+ * forward op: runs warmup + steps matvecs on the provider's stream and
+ * reports, per timed step, the CUDA-event time of the whole step and of the
+ * tiled kernel(s) alone, and the number of kernels launched. With flush_l2
+ * a 256 MB buffer is rewritten before every step (outside the timed events). */
+int gpb_benchmark_forward(gpb_provider* p, const float* v_dev, float* out_dev, int64_t ncols,
+                          int32_t warmup, int32_t steps, int32_t flush_l2, double* step_ms_out,
+                          double* kernel_ms_out, int64_t* launches_out);
+
+/* FP32 (FFMA) throughput probe on `device`: the measured denominator of the
+ * matvec roofline. No reference counterpart (measurement utility). */
+int gpb_measure_fp32_peak(int32_t device, double* tflops_out, double* ms_out);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* GPB200_H */

@@ -1,0 +1,96 @@
+// Instantiation helper: compiles the tile kernel for every supported (DP, T)
+// of one evaluator and launches the requested one.
+#pragma once
+
+#include "kv_launch.cuh"
+
+namespace gpb {
+
+template <int DP, int T, class Ev>
+int kv_launch_one(const KvLaunch& L) {
+  constexpr bool kGen = Ev::kGeneric;
+  constexpr int R = kv_rows_per_thread(DP, T, kGen);
+  constexpr int W = packed_width(DP, T);
+  auto kern = kv_tile_kernel<DP, T, R, kKvBlock, Ev>;
+  const size_t smem = (size_t)kStages * kJT * W * sizeof(float);
+
+  int dev = 0;
+  GPB_CHECK_CUDA(cudaGetDevice(&dev));
+  static int resident[64];
+  static bool init[64] = {false};
+  static int num_sms[64];
+  if (dev < 0 || dev >= 64) dev = 0;
+  if (!init[dev]) {
+    GPB_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    GPB_CHECK_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&resident[dev], kern, kKvBlock, smem));
+    GPB_CHECK_CUDA(cudaDeviceGetAttribute(&num_sms[dev], cudaDevAttrMultiProcessorCount, dev));
+    if (resident[dev] < 1) resident[dev] = 1;
+    init[dev] = true;
+  }
+  const int64_t rows_per_block = (int64_t)kKvBlock * R;
+  const int64_t row_blocks = ceil_div(L.nrow, rows_per_block);
+  if (row_blocks == 0 || L.ntiles == 0) return GPB_OK;
+  GPB_REQUIRE(row_blocks < (1ll << 31), GPB_ERR_INVALID, "too many rows for one launch: %lld",
+              (long long)L.nrow);
+  int splits = kv_choose_splits(row_blocks, L.ntiles, resident[dev], num_sms[dev]);
+  if (splits > 1) {
+    const int64_t need_per_split = (int64_t)T * L.nrow;
+    const int64_t cap = L.partial ? L.partial_capacity / need_per_split : 0;
+    if (cap < splits) splits = (int)(cap >= 2 ? cap : 1);
+  }
+  int tiles_per_split = (int)ceil_div(L.ntiles, splits);
+  splits = (int)ceil_div(L.ntiles, tiles_per_split);
+
+  TileEpilogue ep = L.ep;
+  ep.tcols = L.tcols;
+  if (splits > 1) {
+    ep.out = L.partial;
+    ep.out_ld = L.nrow;
+  }
+  dim3 grid((unsigned)row_blocks, (unsigned)splits);
+  typename Ev::Params params;
+  if constexpr (kGen) {
+    params = *L.dk;
+  } else {
+    params = L.fp;
+  }
+  if (L.ev_begin) GPB_CHECK_CUDA(cudaEventRecord(L.ev_begin, L.stream));
+  kern<<<grid, kKvBlock, smem, L.stream>>>(L.xrow, L.nrow, L.xv, L.ntiles, tiles_per_split, params,
+                                           ep, L.err);
+  GPB_CHECK_CUDA(cudaGetLastError());
+  if (L.launches) *L.launches += 1;
+  if (splits > 1) {
+    GPB_TRY(launch_kv_reduce(L, splits));
+    if (L.launches) *L.launches += 1;
+  }
+  if (L.ev_end) GPB_CHECK_CUDA(cudaEventRecord(L.ev_end, L.stream));
+  return GPB_OK;
+}
+
+template <int DP, class Ev>
+int kv_launch_t(const KvLaunch& L) {
+  switch (L.T) {
+    case 1: return kv_launch_one<DP, 1, Ev>(L);
+    case 4: return kv_launch_one<DP, 4, Ev>(L);
+    case 8: return kv_launch_one<DP, 8, Ev>(L);
+    case 16: return kv_launch_one<DP, 16, Ev>(L);
+  }
+  set_error("unsupported rhs tile width T=%d", L.T);
+  return GPB_ERR_UNSUPPORTED;
+}
+
+template <class Ev>
+int kv_launch_fast(const KvLaunch& L) {
+  switch (L.DP) {
+    case 1: return kv_launch_t<1, Ev>(L);
+    case 2: return kv_launch_t<2, Ev>(L);
+    case 4: return kv_launch_t<4, Ev>(L);
+    case 8: return kv_launch_t<8, Ev>(L);
+    case 16: return kv_launch_t<16, Ev>(L);
+    case 32: return kv_launch_t<32, Ev>(L);
+  }
+  set_error("unsupported padded dimension DP=%d", L.DP);
+  return GPB_ERR_UNSUPPORTED;
+}
+
+}  // namespace gpb

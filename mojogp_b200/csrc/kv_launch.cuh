@@ -1,0 +1,82 @@
+// Host-side launch description for the tiled matvec and the per-evaluator
+// dispatch over the compiled (DP, T) instantiations.
+#pragma once
+
+#include "kv_tiles.cuh"
+
+namespace gpb {
+
+// Evaluator ids: the five fast leaves use their GPB_KERNEL_* value,
+// kEvalGeneric selects the tree evaluator.
+constexpr int kEvalGeneric = 100;
+
+struct KvLaunch {
+  int eval;                 // GPB_KERNEL_RBF..RQ or kEvalGeneric
+  int DP;                   // padded dims of xrow / packed x (compiled sizes only)
+  int T;                    // rhs columns per pass (compiled sizes only)
+  const float* xrow;        // [nrow][DP]
+  int64_t nrow;
+  const float* xv;          // packed [ntiles*kJT][packed_width(DP,T)]
+  int ntiles;
+  FastParams fp;
+  const DevKernel* dk;      // generic evaluator program (host copy, passed by value)
+  TileEpilogue ep;          // ep.out = final output (column stride ep.out_ld)
+  int tcols;                // valid columns (<= T)
+  float* partial;           // scratch for split partial sums (may be null if splits==1)
+  int64_t partial_capacity; // floats available in `partial`
+  int* err;                 // device error word
+  cudaStream_t stream;
+  int64_t* launches = nullptr;      // incremented per kernel launched
+  cudaEvent_t ev_begin = nullptr;   // if set: recorded around the tile kernel(s)
+  cudaEvent_t ev_end = nullptr;
+};
+
+// Compiled sizes.
+inline bool kv_dp_supported(int eval, int DP) {
+  if (eval == kEvalGeneric) return DP == 4 || DP == 8 || DP == 16 || DP == 32 || DP == 64;
+  return DP == 1 || DP == 2 || DP == 4 || DP == 8 || DP == 16 || DP == 32;
+}
+inline int kv_pick_dp(int eval, int d) {
+  const int cand_fast[] = {1, 2, 4, 8, 16, 32};
+  const int cand_gen[] = {4, 8, 16, 32, 64};
+  if (eval == kEvalGeneric) {
+    for (int c : cand_gen)
+      if (d <= c) return c;
+  } else {
+    for (int c : cand_fast)
+      if (d <= c) return c;
+  }
+  return -1;
+}
+inline int kv_pick_t(int64_t remaining) {
+  if (remaining >= 16) return 16;
+  if (remaining > 8) return 16;
+  if (remaining > 4) return 8;
+  if (remaining > 1) return 4;
+  return 1;
+}
+
+// Rows per thread for a (DP, T, generic) instantiation.
+__host__ __device__ constexpr int kv_rows_per_thread(int DP, int T, bool generic) {
+  return generic ? 1 : (DP >= 32 ? 2 : 4);
+}
+constexpr int kKvBlock = 128;
+
+// Per-evaluator launchers (one translation unit each).
+int launch_kv_rbf(const KvLaunch& L);
+int launch_kv_m12(const KvLaunch& L);
+int launch_kv_m32(const KvLaunch& L);
+int launch_kv_m52(const KvLaunch& L);
+int launch_kv_rq(const KvLaunch& L);
+int launch_kv_generic(const KvLaunch& L);
+
+int launch_kv(const KvLaunch& L);
+
+// Choose the number of j-splits for `row_blocks` row tiles so that the grid
+// fills the GPU's resident slots with little wave-quantisation loss.
+int kv_choose_splits(int64_t row_blocks, int ntiles, int resident_per_sm, int num_sms);
+
+// Deterministic fixed-order reduction of split partials + epilogue.
+int launch_kv_reduce(const KvLaunch& L, int splits);
+
+}  // namespace gpb

@@ -1,0 +1,114 @@
+// Matvec plumbing: split selection, deterministic split reduction, input
+// prescaling and column packing for the tiled K·V kernels.
+#include "kv_launch.cuh"
+#include "matvec.cuh"
+
+namespace gpb {
+
+int launch_kv(const KvLaunch& L) {
+  switch (L.eval) {
+    case GPB_KERNEL_RBF: return launch_kv_rbf(L);
+    case GPB_KERNEL_MATERN12: return launch_kv_m12(L);
+    case GPB_KERNEL_MATERN32: return launch_kv_m32(L);
+    case GPB_KERNEL_MATERN52: return launch_kv_m52(L);
+    case GPB_KERNEL_RQ: return launch_kv_rq(L);
+    case kEvalGeneric: return launch_kv_generic(L);
+  }
+  set_error("unknown evaluator %d", L.eval);
+  return GPB_ERR_INVALID;
+}
+
+int kv_choose_splits(int64_t row_blocks, int ntiles, int resident_per_sm, int num_sms) {
+  const int64_t slots = (int64_t)resident_per_sm * num_sms;
+  // Each split should still stream a handful of tiles through the TMA ring.
+  const int max_by_tiles = ntiles / 4 > 1 ? ntiles / 4 : 1;
+  int best = 1;
+  double best_cost = 1e300;
+  for (int s = 1; s <= 32 && s <= max_by_tiles; ++s) {
+    const int64_t blocks = row_blocks * s;
+    const int64_t waves = ceil_div(blocks, slots);
+    // time ~ waves * (work per block) ~ waves / s; small penalty per split
+    // for the partial-sum traffic and reduction.
+    const double cost = (double)waves / s * (1.0 + 0.004 * (s - 1));
+    if (cost < best_cost * 0.995) {
+      best_cost = cost;
+      best = s;
+    }
+  }
+  return best;
+}
+
+__global__ void kv_reduce_kernel(const float* __restrict__ part, int splits, int T, int tcols,
+                                 int64_t nrow, TileEpilogue ep) {
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t total = (int64_t)tcols * nrow;
+  if (idx >= total) return;
+  const int c = (int)(idx / nrow);
+  const int64_t i = idx - (int64_t)c * nrow;
+  float s = 0.f;
+  for (int sp = 0; sp < splits; ++sp) s += part[((int64_t)sp * T + c) * nrow + i];
+  float o = ep.scale * s;
+  if (ep.noise_v) {
+    const float nz = ep.noise_vec ? ep.noise_vec[i] : ep.noise;
+    o = fmaf(nz, ep.noise_v[c * ep.noise_ld + i], o);
+  }
+  ep.out[c * ep.out_ld + i] = o;
+}
+
+int launch_kv_reduce(const KvLaunch& L, int splits) {
+  const int64_t total = (int64_t)L.tcols * L.nrow;
+  if (total == 0) return GPB_OK;
+  const int bs = 256;
+  kv_reduce_kernel<<<(unsigned)ceil_div(total, bs), bs, 0, L.stream>>>(L.partial, splits, L.T,
+                                                                      L.tcols, L.nrow, L.ep);
+  GPB_CHECK_CUDA(cudaGetLastError());
+  return GPB_OK;
+}
+
+// xs[i][k] = X[i][dims[k]] * scale[k] for k < nd, 0 for nd <= k < DP.
+__global__ void prescale_kernel(const float* __restrict__ X, int64_t n, int d, PrescaleSpec ps,
+                                float* __restrict__ xs) {
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t total = n * ps.DP;
+  if (idx >= total) return;
+  const int64_t i = idx / ps.DP;
+  const int k = (int)(idx - i * ps.DP);
+  xs[idx] = (k < ps.nd) ? X[i * d + ps.dims[k]] * ps.scale[k] : 0.f;
+}
+
+int launch_prescale(const float* X, int64_t n, int d, const PrescaleSpec& ps, float* xs,
+                    cudaStream_t stream) {
+  const int64_t total = n * ps.DP;
+  if (total == 0) return GPB_OK;
+  prescale_kernel<<<(unsigned)ceil_div(total, 256), 256, 0, stream>>>(X, n, d, ps, xs);
+  GPB_CHECK_CUDA(cudaGetLastError());
+  return GPB_OK;
+}
+
+// Packed column rows: xv[j] = [xs[j][0..DP), v[c0+c][j] for c < tcols, 0...]
+// for j < n, zero rows for n <= j < npad (their v = 0, so they add nothing).
+__global__ void pack_kernel(const float* __restrict__ xs, int DP, const float* __restrict__ v,
+                            int64_t v_ld, int tcols, int64_t n, int64_t npad, int W,
+                            float* __restrict__ xv) {
+  const int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (j >= npad) return;
+  float* row = xv + j * W;
+  if (j < n) {
+    for (int k = 0; k < DP; ++k) row[k] = xs[j * DP + k];
+    for (int c = 0; c < W - DP; ++c) row[DP + c] = (c < tcols) ? v[c * v_ld + j] : 0.f;
+  } else {
+    for (int k = 0; k < W; ++k) row[k] = 0.f;
+  }
+}
+
+int launch_pack(const float* xs, int DP, const float* v, int64_t v_ld, int tcols, int T, int64_t n,
+                int64_t npad, float* xv, cudaStream_t stream) {
+  const int W = packed_width(DP, T);
+  if (npad == 0) return GPB_OK;
+  pack_kernel<<<(unsigned)ceil_div(npad, 256), 256, 0, stream>>>(xs, DP, v, v_ld, tcols, n, npad,
+                                                                W, xv);
+  GPB_CHECK_CUDA(cudaGetLastError());
+  return GPB_OK;
+}
+
+}  // namespace gpb
