@@ -171,6 +171,98 @@ int gpb_benchmark_forward(gpb_provider* p, const float* v_dev, float* out_dev, i
  * matvec roofline. No reference counterpart (measurement utility). */
 int gpb_measure_fp32_peak(int32_t device, double* tflops_out, double* ms_out);
 
+/* ------------------------------------------------------- multi-GPU comm
+ * One communicator per process-per-GPU (NCCL over NVLink/NVSwitch). The
+ * 128-byte unique id is created on rank 0 (gpb_comm_unique_id) and shared
+ * with the other ranks by the host (any transport), then every rank calls
+ * gpb_comm_init. No reference counterpart: MojoGP is single-GPU. */
+typedef struct gpb_comm gpb_comm;
+#define GPB_COMM_ID_BYTES 128
+int gpb_comm_unique_id(uint8_t* id_out /* GPB_COMM_ID_BYTES */);
+int gpb_comm_init(const uint8_t* id, int32_t world, int32_t rank, int32_t device, gpb_comm** out);
+int gpb_comm_destroy(gpb_comm* c);
+/* Host-value collectives for harness use (timing max, barriers). */
+int gpb_comm_allreduce_max_f64(gpb_comm* c, double* value_inout);
+int gpb_comm_allreduce_sum_f64(gpb_comm* c, double* values_inout, int64_t count);
+int gpb_comm_barrier(gpb_comm* c);
+/* Row-sharded forward matvec benchmark: each rank computes rows
+ * [n*rank/world, n*(rank+1)/world) of (K + noise) V and all-gathers the packed
+ * output blocks, i.e. one CG-iteration matvec. Same outputs as
+ * gpb_benchmark_forward. */
+int gpb_benchmark_forward_sharded(gpb_provider* p, gpb_comm* c, const float* v_dev, int64_t ncols,
+                                  int32_t warmup, int32_t steps, int32_t flush_l2,
+                                  double* step_ms_out, double* kernel_ms_out,
+                                  int64_t* launches_out);
+
+/* ------------------------------------------------------------- training
+ * Replaces engine.train (jit_engine_bindings.mojo:123-432 ->
+ * jit_training.mojo:274-1008): Adam over softplus-raw kernel params, noise and
+ * a constant mean; per iteration one BBMM step (probes, mBCG with tridiagonal
+ * capture, SLQ log-det, fused gradient reduction) with a greedy pivoted-
+ * Cholesky preconditioner rebuilt when parameters move by more than
+ * precond_rebuild_threshold. With comm != NULL the rows are sharded. */
+typedef struct {
+  int32_t max_iterations;
+  float learning_rate;
+  int32_t num_probes;
+  int32_t max_cg_iter;
+  float cg_tol;
+  int32_t precond_rank;
+  int32_t max_tridiag_iter;
+  float precond_rebuild_threshold;
+  int32_t use_cosine_lr;
+  int32_t use_preconditioner;
+  int32_t learn_noise;
+  float init_mean;
+  int32_t enable_early_stopping;
+  int32_t early_stop_patience;
+  float early_stop_tol;
+  int32_t verbose;
+  const uint8_t* trainable_mask; /* num_params entries (1 = train) or NULL */
+} gpb_train_options;
+
+typedef struct {
+  float final_nll;       /* best NLL seen (per sample) */
+  float noise;
+  float mean;
+  int32_t iterations;
+  int32_t converged;
+  float* params;         /* [num_params], caller-allocated */
+  float* nll_history;    /* [max_iterations] */
+  double* iter_times_ms; /* [max_iterations] */
+  int32_t* cg_iterations;/* [max_iterations] */
+  float* alpha;          /* [n] best-iteration (K + noise)^{-1}(y - mean), or NULL */
+  int32_t alpha_valid;
+  int32_t precond_build_count;
+  double precond_build_ms;
+  int32_t precond_rank;
+} gpb_train_result;
+
+int gpb_train(gpb_provider* p, gpb_comm* comm, const float* y_host, int64_t n,
+              const gpb_train_options* opt, gpb_train_result* res);
+
+/* One BBMM evaluation at the provider's current parameters (no optimizer
+ * step): NLL and gradients w.r.t. the constrained kernel params and noise.
+ * Replaces bbmm_with_precond (combined_inv_quad_logdet.mojo:452-1136). grads
+ * has num_params + 1 entries (noise last). */
+int gpb_bbmm(gpb_provider* p, gpb_comm* comm, const float* y_centered_host, int64_t n,
+             int32_t num_probes, int32_t max_cg_iter, int32_t max_tridiag_iter, float cg_tol,
+             int32_t precond_rank, int32_t iteration, double* nll_out, double* grads_out,
+             double* logdet_out, double* inv_quad_out, int32_t* cg_iters_out);
+
+/* Host-only numerics exposed for testing (no GPU needed): the SLQ
+ * log-determinant from per-probe tridiagonals (diags [num_probes][m],
+ * offdiags [num_probes][m-1]; native_numerics.mojo:403-518) and the
+ * symmetric tridiagonal eigensolver (native_numerics.mojo:724-849). */
+int gpb_slq_logdet(const double* diags, const double* offdiags, int32_t m, int32_t num_probes,
+                   int64_t n, double* out);
+int gpb_tridiag_eig(const double* diag, const double* offdiag, int32_t m, double* evals,
+                    double* evecs);
+
+/* Replaces kernel_gpu_gaussian (pivoted_cholesky.mojo:51-86): counter-hash
+ * Box-Muller normals for indices [0, count) with `seed`, copied to host. */
+int gpb_hash_gaussian(int32_t device, float* out_host, int64_t count, uint64_t seed);
+
 #ifdef __cplusplus
 }
 #endif

@@ -54,6 +54,18 @@ SIGNATURES = {
     "gpb_gradient_bilinear": [P, P, P, c_i64, P, P],
     "gpb_benchmark_forward": [P, P, P, c_i64, c_i32, c_i32, c_i32, P, P, P],
     "gpb_measure_fp32_peak": [c_i32, PD, PD],
+    "gpb_comm_unique_id": [P],
+    "gpb_comm_init": [P, c_i32, c_i32, c_i32, PP],
+    "gpb_comm_destroy": [P],
+    "gpb_comm_allreduce_max_f64": [P, PD],
+    "gpb_comm_allreduce_sum_f64": [P, P, c_i64],
+    "gpb_comm_barrier": [P],
+    "gpb_benchmark_forward_sharded": [P, P, P, c_i64, c_i32, c_i32, c_i32, P, P, P],
+    "gpb_train": [P, P, P, c_i64, P, P],
+    "gpb_bbmm": [P, P, P, c_i64, c_i32, c_i32, c_i32, c_f32, c_i32, c_i32, P, P, P, P, P],
+    "gpb_slq_logdet": [P, P, c_i32, c_i32, c_i64, P],
+    "gpb_tridiag_eig": [P, P, c_i32, P, P],
+    "gpb_hash_gaussian": [c_i32, P, c_i64, C.c_uint64],
 }
 _RESTYPES = {"gpb_version": C.c_char_p}
 

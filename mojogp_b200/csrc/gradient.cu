@@ -416,7 +416,7 @@ int provider_bilinear_rows(gpb_provider* p, const float* a_dev, int64_t a_ld, co
     GPB_TRY(p->ws.get(WS_GRAD, (size_t)cap * sizeof(float) + 4096, &part));
     int64_t nb = 0;
     const int has_data = c0 == 0 ? 1 : 0;
-    const float* a_chunk = a_dev + c0 * a_ld + row_begin;
+    const float* a_chunk = a_dev + c0 * a_ld;  // a_dev points at row_begin
     int s;
     switch (p->eval) {
       case GPB_KERNEL_RBF:
@@ -522,7 +522,7 @@ int gpb_gradient_bilinear(gpb_provider* p, const float* a_dev, const float* b_de
               "bad arguments");
   GPB_CHECK_CUDA(cudaSetDevice(p->device));
   GPB_TRY(provider_bilinear_rows(p, a_dev, p->n, b_dev, ncols, 0, p->n, data_out, trace_out,
-                                 p->stream));
+                                 p->stream));  // a at row 0
   return provider_check_device_error(p);
 }
 

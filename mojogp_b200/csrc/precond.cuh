@@ -1,0 +1,23 @@
+// Pivoted-Cholesky preconditioner state and operations (see precond.cu).
+#pragma once
+
+#include "engine.cuh"
+
+namespace gpb {
+
+struct Precond {
+  int rank = 0;        // actual rank; 0 = no preconditioner
+  float noise = 0.f;
+  double logdet = 0.0;  // log|L L^T + noise I|
+  DBuf L;               // [rank][nl] (column k of L over this rank's rows)
+  DBuf Minv;            // [rank][rank] float
+  DBuf u;               // [t][rank] work
+  DBuf diag, mask, scratch, keys;
+};
+
+int precond_build(Engine& E, int rank_req, Precond& P);
+int precond_finalize(Engine& E, Precond& P);
+int precond_apply(Engine& E, Precond& P, const float* v, float* out, int t);
+int precond_sample(Engine& E, Precond& P, int num, uint64_t seed, float* out);
+
+}  // namespace gpb

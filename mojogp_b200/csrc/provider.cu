@@ -119,6 +119,14 @@ int parse_spec(const int32_t* spec, int32_t len, int32_t d, DevKernel* k) {
 // ------------------------------------------------------------------ plan
 int provider_plan(gpb_provider* p) {
   const DevKernel& K = p->dk;
+  for (int l = 0; l < K.nleaves; ++l) {
+    const LeafDesc& L = K.leaf[l];
+    if (L.type == GPB_KERNEL_POLYNOMIAL) {
+      const float deg = K.params[L.pofs + (L.ard ? L.ndims : 0)];
+      GPB_REQUIRE(deg >= 1.f && std::fabs(deg - std::nearbyint(deg)) <= 1e-5f, GPB_ERR_INVALID,
+                  "Polynomial kernel degree must be a fixed positive integer, got %g", (double)deg);
+    }
+  }
   // Fast path: one stationary leaf, optionally under a scale node.
   int leaf_node = -1, scale_param = -1;
   if (K.nnodes == 1 && K.node_op[0] == GPB_NODE_LEAF) leaf_node = 0;

@@ -79,6 +79,7 @@ int provider_prescale_rows(gpb_provider* p, const float* x_raw, int64_t nrow, in
                            const float** out, cudaStream_t stream);
 
 // Bilinear gradient sums over rows [row_begin, row_end) (see gradient.cu).
+// a_dev points at row row_begin (column stride a_ld); b_dev holds all n rows.
 int provider_bilinear_rows(gpb_provider* p, const float* a_dev, int64_t a_ld, const float* b_dev,
                            int64_t ncols, int64_t row_begin, int64_t row_end, double* data_out,
                            double* trace_out, cudaStream_t st);

@@ -1,0 +1,131 @@
+"""Engine protocol over the C ABI: train / bbmm / predict.
+
+Keeps the reference engine's call shapes and result-dict keys
+(mojogp/kernels/jit/jit_engine_bindings.mojo:123-432 train, 944-1234 predict,
+636-942 prediction cache) so the orchestration in gp.py reads like the
+reference's gp.py:1608-2047.
+"""
+from __future__ import annotations
+
+import ctypes as C
+from typing import Optional
+
+import numpy as np
+
+from . import _lib
+from .provider import Provider
+
+
+class TrainOptions(C.Structure):
+    _fields_ = [
+        ("max_iterations", C.c_int32),
+        ("learning_rate", C.c_float),
+        ("num_probes", C.c_int32),
+        ("max_cg_iter", C.c_int32),
+        ("cg_tol", C.c_float),
+        ("precond_rank", C.c_int32),
+        ("max_tridiag_iter", C.c_int32),
+        ("precond_rebuild_threshold", C.c_float),
+        ("use_cosine_lr", C.c_int32),
+        ("use_preconditioner", C.c_int32),
+        ("learn_noise", C.c_int32),
+        ("init_mean", C.c_float),
+        ("enable_early_stopping", C.c_int32),
+        ("early_stop_patience", C.c_int32),
+        ("early_stop_tol", C.c_float),
+        ("verbose", C.c_int32),
+        ("trainable_mask", C.c_void_p),
+    ]
+
+
+class TrainResult(C.Structure):
+    _fields_ = [
+        ("final_nll", C.c_float),
+        ("noise", C.c_float),
+        ("mean", C.c_float),
+        ("iterations", C.c_int32),
+        ("converged", C.c_int32),
+        ("params", C.c_void_p),
+        ("nll_history", C.c_void_p),
+        ("iter_times_ms", C.c_void_p),
+        ("cg_iterations", C.c_void_p),
+        ("alpha", C.c_void_p),
+        ("alpha_valid", C.c_int32),
+        ("precond_build_count", C.c_int32),
+        ("precond_build_ms", C.c_double),
+        ("precond_rank", C.c_int32),
+    ]
+
+
+def _p(a: np.ndarray) -> C.c_void_p:
+    return C.c_void_p(a.ctypes.data)
+
+
+def train(provider: Provider, y: np.ndarray, *, max_iterations: int = 100,
+          learning_rate: float = 0.01, num_probes: int = 10, max_cg_iter: int = 100,
+          cg_tol: float = 1e-2, precond_rank: int = 100, max_tridiag_iter: int = 30,
+          precond_rebuild_threshold: float = 0.5, use_cosine_lr: bool = False,
+          use_preconditioner: bool = True, learn_noise: bool = True, init_mean: float = 0.0,
+          enable_early_stopping: bool = False, early_stop_patience: int = 10,
+          early_stop_tol: float = 1e-4, verbose: bool = False,
+          trainable_mask: Optional[np.ndarray] = None, comm=None) -> dict:
+    """Run the training loop on the device; returns the reference's result keys."""
+    y = np.ascontiguousarray(y, dtype=np.float32).ravel()
+    if y.shape[0] != provider.n:
+        raise ValueError(f"y has {y.shape[0]} rows, provider has {provider.n}")
+    P = provider.num_params
+    mask = None
+    if trainable_mask is not None:
+        mask = np.ascontiguousarray(trainable_mask, dtype=np.uint8)
+    opt = TrainOptions(max_iterations, learning_rate, num_probes, max_cg_iter, cg_tol,
+                       precond_rank, max_tridiag_iter, precond_rebuild_threshold,
+                       int(use_cosine_lr), int(use_preconditioner), int(learn_noise), init_mean,
+                       int(enable_early_stopping), early_stop_patience, early_stop_tol,
+                       int(verbose), _p(mask) if mask is not None else None)
+    params = np.zeros(P, np.float32)
+    nll_hist = np.full(max(max_iterations, 1), np.nan, np.float32)
+    times = np.zeros(max(max_iterations, 1), np.float64)
+    cg_it = np.zeros(max(max_iterations, 1), np.int32)
+    alpha = np.zeros(provider.n, np.float32)
+    res = TrainResult()
+    res.params = _p(params).value
+    res.nll_history = _p(nll_hist).value
+    res.iter_times_ms = _p(times).value
+    res.cg_iterations = _p(cg_it).value
+    res.alpha = _p(alpha).value
+    _lib.call("gpb_train", provider.h, C.c_void_p(comm.handle) if comm else None, _p(y),
+              provider.n, C.byref(opt), C.byref(res))
+    it = int(res.iterations)
+    provider._params = params.copy()
+    provider._noise = float(res.noise)
+    return {
+        "final_nll": float(res.final_nll),
+        "noise": float(res.noise),
+        "mean": float(res.mean),
+        "iterations": it,
+        "converged": bool(res.converged),
+        "params": params,
+        "iter_times_ms": times[:it].copy(),
+        "nll_history": nll_hist[:it].copy(),
+        "cg_iterations_history": cg_it[:it].copy(),
+        "cached_alpha": alpha if res.alpha_valid else None,
+        "precond_build_count": int(res.precond_build_count),
+        "precond_build_time_ms": float(res.precond_build_ms),
+        "precond_rank": int(res.precond_rank),
+    }
+
+
+def bbmm(provider: Provider, y_centered: np.ndarray, *, num_probes: int = 10,
+         max_cg_iter: int = 100, max_tridiag_iter: int = 30, cg_tol: float = 1e-2,
+         precond_rank: int = 0, iteration: int = 0, comm=None) -> dict:
+    """One NLL + gradient evaluation at the provider's parameters."""
+    y = np.ascontiguousarray(y_centered, dtype=np.float32).ravel()
+    nll = C.c_double()
+    grads = np.zeros(provider.num_params + 1, np.float64)
+    ld, iq = C.c_double(), C.c_double()
+    it = C.c_int32()
+    _lib.call("gpb_bbmm", provider.h, C.c_void_p(comm.handle) if comm else None, _p(y),
+              provider.n, num_probes, max_cg_iter, max_tridiag_iter, float(cg_tol), precond_rank,
+              iteration, C.byref(nll), _p(grads), C.byref(ld), C.byref(iq), C.byref(it))
+    return {"nll": nll.value, "grads": grads, "logdet": ld.value, "inv_quad": iq.value,
+            "cg_iters": it.value}

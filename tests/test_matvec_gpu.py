@@ -38,10 +38,10 @@ def _params(k, d, rng):
     p = rng.uniform(0.5, 2.0, size=kk.num_params()).astype(np.float32)
     names = kk.get_param_names()
     for i, nm in enumerate(names):
-        if nm.endswith("degree"):
-            p[i] = 2.0
         if "linear" in nm or "polynomial" in nm:
             p[i] = rng.uniform(0.2, 0.6)
+        if nm.endswith("degree"):
+            p[i] = 2.0
     return kk, p
 
 
