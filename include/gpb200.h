@@ -263,6 +263,31 @@ int gpb_tridiag_eig(const double* diag, const double* offdiag, int32_t m, double
  * Box-Muller normals for indices [0, count) with `seed`, copied to host. */
 int gpb_hash_gaussian(int32_t device, float* out_host, int64_t count, uint64_t seed);
 
+/* ----------------------------------------------------------- prediction
+ * Replaces the engine's alpha solve (jit_prediction.mojo:681-806): CG on
+ * (K + noise I) alpha = y - mean with the relative-residual stop rule.
+ * alpha_host_out has n entries (all rows, also when sharded). */
+int gpb_compute_alpha(gpb_provider* p, gpb_comm* comm, const float* y_centered_host, int64_t n,
+                      int32_t max_cg_iter, float cg_tol, float* alpha_host_out,
+                      int32_t* iters_out);
+
+/* Replaces prepare_prediction_cache / predict_with_cache /
+ * destroy_prediction_cache (jit_engine_bindings.mojo:636-942): holds alpha and
+ * the LOVE inverse root S ([love_rank][n], S S^T ~ (K + noise I)^{-1},
+ * jit_prediction.mojo:974-1177) on the device. root_host may supply a
+ * previously exported root; NULL computes it (Lanczos with full
+ * re-orthogonalisation). love_rank 0 = mean only. */
+typedef struct gpb_prediction_cache gpb_prediction_cache;
+int gpb_prediction_cache_create(gpb_provider* p, gpb_comm* comm, const float* alpha_host,
+                                float mean, int32_t love_rank, const float* root_host,
+                                gpb_prediction_cache** out);
+int gpb_prediction_cache_root(gpb_prediction_cache* c, float* root_host_out);
+/* mean = K(X*, X) alpha + mean; var = max(k** - |K(X*, X) S|^2, 1e-10) + noise
+ * (jit_prediction.mojo:211-232, 1236-1344, 2048-2051). var_out may be NULL. */
+int gpb_predict_with_cache(gpb_prediction_cache* c, const float* xtest_host, int64_t n_test,
+                           float* mean_out, float* var_out);
+int gpb_prediction_cache_destroy(gpb_prediction_cache* c);
+
 #ifdef __cplusplus
 }
 #endif

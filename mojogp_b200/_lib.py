@@ -66,6 +66,11 @@ SIGNATURES = {
     "gpb_slq_logdet": [P, P, c_i32, c_i32, c_i64, P],
     "gpb_tridiag_eig": [P, P, c_i32, P, P],
     "gpb_hash_gaussian": [c_i32, P, c_i64, C.c_uint64],
+    "gpb_compute_alpha": [P, P, P, c_i64, c_i32, c_f32, P, PI32],
+    "gpb_prediction_cache_create": [P, P, P, c_f32, c_i32, P, PP],
+    "gpb_prediction_cache_root": [P, P],
+    "gpb_predict_with_cache": [P, P, c_i64, P, P],
+    "gpb_prediction_cache_destroy": [P],
 }
 _RESTYPES = {"gpb_version": C.c_char_p}
 

@@ -101,6 +101,9 @@ int k_woodbury_out(const float* v, int64_t ld, const float* L, int64_t nl, int r
                    const float* u, int t, float inv_noise, float* out, cudaStream_t st);
 int k_minv_apply(const float* Minv, int rank, const double* w, int t, float* u, cudaStream_t st);
 int k_ltl(const float* L, int64_t nl, int rank, Reducer& red, cudaStream_t st);
+// out[c][i] = add_coef * src[c][i] + lu_coef * sum_k L[k][i] u[c][k]
+int k_l_times_u(const float* L, int64_t nl, int rank, const float* u, int t, const float* src,
+                int64_t ld, float add_coef, float lu_coef, float* out, cudaStream_t st);
 int k_lz_plus_noise(const float* L, int64_t nl, int rank, const float* zr, int t,
                     const float* zn, float sqrt_noise, float* out, cudaStream_t st);
 

@@ -444,6 +444,16 @@ int k_woodbury_out(const float* v, int64_t ld, const float* L, int64_t nl, int r
   return GPB_OK;
 }
 
+int k_l_times_u(const float* L, int64_t nl, int rank, const float* u, int t, const float* src,
+                int64_t ld, float add_coef, float lu_coef, float* out, cudaStream_t st) {
+  if (nl <= 0) return GPB_OK;
+  const size_t smem = (size_t)t * rank * sizeof(float);
+  l_times_u_kernel<<<(unsigned)ceil_div(nl, 256), 256, smem, st>>>(L, nl, rank, u, t, src, ld,
+                                                                  add_coef, lu_coef, out);
+  GPB_CHECK_CUDA(cudaGetLastError());
+  return GPB_OK;
+}
+
 int k_lz_plus_noise(const float* L, int64_t nl, int rank, const float* zr, int t, const float* zn,
                     float sqrt_noise, float* out, cudaStream_t st) {
   if (nl <= 0) return GPB_OK;

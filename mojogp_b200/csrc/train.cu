@@ -512,7 +512,8 @@ int train_loop(Engine& E, const float* y_host_local, const gpb_train_options& o,
 
 using namespace gpb;
 
-static int make_engine(gpb_provider* p, gpb_comm* comm, Engine& E) {
+namespace gpb {
+int engine_from_comm(gpb_provider* p, gpb_comm* comm, Engine& E) {
   Dist d;
   if (comm) {
     d = comm->dist;
@@ -521,6 +522,7 @@ static int make_engine(gpb_provider* p, gpb_comm* comm, Engine& E) {
   }
   return E.init(p, d);
 }
+}  // namespace gpb
 
 extern "C" {
 
@@ -605,7 +607,7 @@ int gpb_train(gpb_provider* p, gpb_comm* comm, const float* y_host, int64_t n,
               GPB_ERR_INVALID, "invalid training options");
   GPB_CHECK_CUDA(cudaSetDevice(p->device));
   Engine E;
-  GPB_TRY(make_engine(p, comm, E));
+  GPB_TRY(engine_from_comm(p, comm, E));
   return train_loop(E, y_host + E.r0, *opt, *res);
 }
 
@@ -618,7 +620,7 @@ int gpb_bbmm(gpb_provider* p, gpb_comm* comm, const float* y_centered_host, int6
   GPB_REQUIRE(n == p->n && num_probes >= 1, GPB_ERR_INVALID, "bad sizes");
   GPB_CHECK_CUDA(cudaSetDevice(p->device));
   Engine E;
-  GPB_TRY(make_engine(p, comm, E));
+  GPB_TRY(engine_from_comm(p, comm, E));
   BBMMState S;
   GPB_TRY(S.ensure(E, 1 + num_probes, max_tridiag_iter));
   GPB_CHECK_CUDA(cudaMemcpyAsync(S.yc.ptr, y_centered_host + E.r0, E.nl * sizeof(float),
@@ -645,7 +647,7 @@ int gpb_benchmark_forward_sharded(gpb_provider* p, gpb_comm* c, const float* v_d
               GPB_ERR_INVALID, "bad benchmark arguments");
   GPB_CHECK_CUDA(cudaSetDevice(p->device));
   Engine E;
-  GPB_TRY(make_engine(p, c, E));
+  GPB_TRY(engine_from_comm(p, c, E));
   // Local row block of V and of the output.
   DBuf vloc, out, flush;
   GPB_TRY(vloc.ensure(E.blk((int)ncols) + 16));

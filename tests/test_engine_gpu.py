@@ -40,20 +40,41 @@ def _problem(kind, n=400, d=2, seed=0):
 
 @pytest.mark.parametrize("kind,rank", [("rbf_ard", 0), ("m52", 0), ("rbf_ard", 15), ("m52", 25)])
 def test_bbmm_vs_oracle(gpb_lib, kind, rank):
+    # A fixed CG budget (tolerance 0, 30 = max_tridiag iterations) so float32
+    # and float64 runs take the same iterations; the convergence rule itself
+    # is covered by test_bbmm_convergence_rule.
     X, y, k, p = _problem(kind)
     noise = 0.05
     yc = y - y.mean()
     prov = Provider(X, k, p, noise)
-    got = engine.bbmm(prov, yc, num_probes=10, max_cg_iter=100, max_tridiag_iter=30, cg_tol=1e-2,
+    got = engine.bbmm(prov, yc, num_probes=10, max_cg_iter=30, max_tridiag_iter=30, cg_tol=0.0,
                       precond_rank=rank, iteration=3)
-    ref = ob.bbmm(k.to_spec(X.shape[1]), p, X, yc, noise, 10, 100, 30, 1e-2, iteration=3,
+    ref = ob.bbmm(k.to_spec(X.shape[1]), p, X, yc, noise, 10, 30, 30, 0.0, iteration=3,
                   precond_rank=rank)
-    assert got["cg_iters"] == ref["cg_iters"]
+    assert got["cg_iters"] == ref["cg_iters"] == 30
     assert abs(got["inv_quad"] - ref["inv_quad"]) < 1e-4 * abs(ref["inv_quad"])
     assert abs(got["logdet"] - ref["logdet"]) < 1e-4 * abs(ref["logdet"])
     assert abs(got["nll"] - ref["nll"]) < 1e-4 * abs(ref["nll"])
     g, rg = got["grads"], ref["grads"]
     np.testing.assert_allclose(g, rg, rtol=0, atol=1e-3 * np.abs(rg).max())
+
+
+def test_bbmm_convergence_rule(gpb_lib):
+    # Well-conditioned problem: both stop at the same check (every 10
+    # iterations after 10, never before max_tridiag - 1).
+    rng = np.random.default_rng(0)
+    n, d = 400, 2
+    X = rng.uniform(0, 1, size=(n, d)).astype(np.float32)
+    y = (np.sin(6 * X[:, 0]) + 0.1 * rng.standard_normal(n)).astype(np.float32)
+    k = make_ard_kernel(RBF(ard=True), d)
+    p = np.array([0.5, 0.5, 1.0], np.float32)
+    yc = y - y.mean()
+    prov = Provider(X, k, p, 0.2)
+    got = engine.bbmm(prov, yc, num_probes=10, max_cg_iter=100, max_tridiag_iter=30, cg_tol=1e-2,
+                      precond_rank=0, iteration=1)
+    ref = ob.bbmm(k.to_spec(d), p, X, yc, 0.2, 10, 100, 30, 1e-2, iteration=1)
+    assert got["cg_iters"] == ref["cg_iters"]
+    assert abs(got["nll"] - ref["nll"]) < 1e-4 * abs(ref["nll"])
 
 
 def test_pivot_order_matches_oracle(gpb_lib):
