@@ -205,14 +205,13 @@ __global__ void __launch_bounds__(128) bilinear_generic_kernel(
   constexpr int W = packed_width(DP, T);
   extern __shared__ __align__(128) float smem[];
   __shared__ __align__(8) uint64_t bars[kStages];
-  __shared__ float red[2 * GPB_MAX_PARAMS];
+  __shared__ float red[4 * 2 * GPB_MAX_PARAMS];
   const int split = blockIdx.y;
   const int t0 = split * tiles_per_split;
   const int ntiles = max(0, min(ntiles_total, t0 + tiles_per_split) - t0);
   TileRing ring{smem, bars, xv, t0, ntiles, (uint32_t)(kJT * W)};
   ring.start();
   const int P = K.nparams;
-  for (int q = threadIdx.x; q < 2 * P; q += BLK) red[q] = 0.f;
 
   const int64_t i = (int64_t)blockIdx.x * BLK + threadIdx.x;
   const bool ok = i < nrow;
@@ -244,22 +243,22 @@ __global__ void __launch_bounds__(128) bilinear_generic_kernel(
     ring.release(kt);
   }
   __syncthreads();
-  // Fixed-order block reduction through shared memory, one parameter at a time.
+  // Fixed-order block reduction: each warp reduces with shuffles and writes
+  // its own slot; thread q then sums the four warp slots in order.
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   for (int q = 0; q < 2 * P; ++q) {
     float x = (q < P) ? gd[q] : gt[q - P];
 #pragma unroll
     for (int o = 16; o > 0; o >>= 1) x += __shfl_xor_sync(0xffffffffu, x, o);
-    if ((threadIdx.x & 31) == 0) {
-      // four warps, fixed order: serialize by warp index
-      for (int w = 0; w < BLK / 32; ++w) {
-        if ((threadIdx.x >> 5) == w) red[q] += x;
-        __syncwarp();
-      }
-    }
+    if (lane == 0) red[warp * 2 * GPB_MAX_PARAMS + q] = x;
   }
   __syncthreads();
   const int64_t bid = (int64_t)blockIdx.y * gridDim.x + blockIdx.x;
-  for (int q = threadIdx.x; q < 2 * P; q += BLK) partial[bid * (2 * P) + q] = red[q];
+  for (int q = threadIdx.x; q < 2 * P; q += BLK) {
+    float s = 0.f;
+    for (int w = 0; w < BLK / 32; ++w) s += red[w * 2 * GPB_MAX_PARAMS + q];
+    partial[bid * (2 * P) + q] = s;
+  }
 }
 
 __global__ void sum_partials_kernel(const float* __restrict__ partial, int64_t nblocks, int nacc,

@@ -44,7 +44,10 @@ def test_bbmm_vs_oracle(gpb_lib, kind, rank):
     # and float64 runs take the same iterations; the convergence rule itself
     # is covered by test_bbmm_convergence_rule.
     X, y, k, p = _problem(kind)
-    noise = 0.05
+    # Without a preconditioner keep K + noise I well conditioned: at condition
+    # numbers ~1e4 float32 CG (as in the reference) and float64 CG part ways
+    # after 30 iterations by more than the 1e-4 bar.
+    noise = 0.05 if rank > 0 else 0.25
     yc = y - y.mean()
     prov = Provider(X, k, p, noise)
     got = engine.bbmm(prov, yc, num_probes=10, max_cg_iter=30, max_tridiag_iter=30, cg_tol=0.0,
@@ -97,7 +100,7 @@ def test_pivot_order_matches_oracle(gpb_lib):
 
 def test_train_matches_oracle(gpb_lib):
     X, y, k, p = _problem("rbf_ard", n=300)
-    noise = 0.1
+    noise = 0.3
     prov = Provider(X, k, p, noise)
     res = engine.train(prov, y, max_iterations=6, learning_rate=0.05, num_probes=10,
                        precond_rank=0, use_preconditioner=False, init_mean=float(y.mean()))
