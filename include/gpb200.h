@@ -288,6 +288,19 @@ int gpb_predict_with_cache(gpb_prediction_cache* c, const float* xtest_host, int
                            float* mean_out, float* var_out);
 int gpb_prediction_cache_destroy(gpb_prediction_cache* c);
 
+/* Same result as gpb_forward_matvec, but the call allocates no device memory:
+ * all scratch lives in one fixed 32 MiB array compiled into the library, held
+ * on every GPU that uses it until the process exits. For callers that must
+ * not allocate while they run (an external memory pool or arena, or code where
+ * an allocation's implicit synchronisation is not allowed). No counterpart in
+ * the reference. Limit: n * DP + round_up(n, 128) * W floats must fit in
+ * 8 Mi floats (DP = padded input dims, W = DP + 16 rounded to 4); larger n is
+ * rejected with GPB_ERR_INVALID. The first call on a device looks up the
+ * array's device address, so make that first call before any stream capture.
+ * Calls share the array: calls that overlap on the GPU race and must be
+ * ordered by the caller. */
+int gpb_forward_matvec_noalloc(gpb_provider* p, float* out_dev, const float* v_dev, int64_t ncols);
+
 #ifdef __cplusplus
 }
 #endif

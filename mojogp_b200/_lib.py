@@ -71,6 +71,7 @@ SIGNATURES = {
     "gpb_prediction_cache_root": [P, P],
     "gpb_predict_with_cache": [P, P, c_i64, P, P],
     "gpb_prediction_cache_destroy": [P],
+    "gpb_forward_matvec_noalloc": [P, P, P, c_i64],
 }
 _RESTYPES = {"gpb_version": C.c_char_p}
 
