@@ -1,0 +1,54 @@
+"""Child script for tests/test_multigpu_gpu.py (one process per GPU).
+
+Every rank holds the same seeded problem; the sharded engine (gpb_comm) must
+reproduce the single-GPU results of rank 0."""
+import json
+import os
+import sys
+from pathlib import Path
+
+import numpy as np
+
+sys.path.insert(0, str(Path(__file__).resolve().parent.parent))
+
+from mojogp_b200 import engine, prediction  # noqa: E402
+from mojogp_b200.distributed import Communicator  # noqa: E402
+from mojogp_b200.kernel import RBF, make_ard_kernel  # noqa: E402
+from mojogp_b200.provider import Provider  # noqa: E402
+
+
+def main(out_path):
+    rank = int(os.environ["RANK"])
+    comm = Communicator.from_env()
+    rng = np.random.default_rng(0)
+    n, d = 3001, 3
+    X = rng.uniform(0, 1, size=(n, d)).astype(np.float32)
+    y = (np.sin(6 * X[:, 0]) + 0.1 * rng.standard_normal(n)).astype(np.float32)
+    k = make_ard_kernel(RBF(ard=True), d)
+    p = np.array([0.4, 0.5, 0.6, 1.0], np.float32)
+    res = {}
+    prov = Provider(X, k, p, 0.1, device=comm.device)
+    yc = y - y.mean()
+    b = engine.bbmm(prov, yc, num_probes=10, max_cg_iter=30, cg_tol=0.0, precond_rank=20,
+                    iteration=2, comm=comm)
+    res["bbmm_nll"] = b["nll"]
+    res["bbmm_grads"] = b["grads"].tolist()
+    tr = engine.train(prov, y, max_iterations=4, learning_rate=0.05, num_probes=10,
+                      precond_rank=20, init_mean=float(y.mean()), comm=comm)
+    res["train_nll"] = tr["nll_history"].tolist()
+    res["train_params"] = tr["params"].tolist()
+    alpha, _ = prediction.compute_alpha(prov, yc, 300, 1e-3, comm=comm)
+    res["alpha_head"] = alpha[:50].tolist()
+    Xs = rng.uniform(0, 1, size=(200, d)).astype(np.float32)
+    cache = prediction.PredictionCache(prov, alpha, float(y.mean()), 40, comm=comm)
+    mean, var = cache.predict(Xs)
+    res["mean"] = mean.tolist()
+    res["var"] = var.tolist()
+    comm.barrier()
+    if rank == 0:
+        Path(out_path).write_text(json.dumps(res))
+    comm.close()
+
+
+if __name__ == "__main__":
+    main(sys.argv[1])

@@ -1,0 +1,53 @@
+"""Row-sharded engine on 2 GPUs (NCCL) vs the same problem on 1 GPU.
+
+Runs tests/mg_worker.py under torchrun as child processes; skipped when fewer
+than 2 GPUs are visible."""
+import json
+import os
+import socket
+import subprocess
+import sys
+from pathlib import Path
+
+import numpy as np
+import pytest
+
+pytestmark = pytest.mark.gpu
+HERE = Path(__file__).resolve().parent
+
+
+def _gpus():
+    from mojogp_b200 import _lib
+    import ctypes as C
+    c = C.c_int32()
+    _lib.lib().gpb_device_count(C.byref(c))
+    return c.value
+
+
+def _run(nproc, out, tmp_path):
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    env = dict(os.environ, NCCL_NVLS_ENABLE="0")
+    cmd = [sys.executable, "-m", "torch.distributed.run", "--nnodes=1", f"--nproc-per-node={nproc}",
+           "--master-addr", "127.0.0.1", "--master-port", str(port), str(HERE / "mg_worker.py"),
+           str(out)]
+    r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=600)
+    assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
+    return json.loads(Path(out).read_text())
+
+
+def test_two_gpu_sharded_engine_matches_one_gpu(gpb_lib, tmp_path):
+    if _gpus() < 2:
+        pytest.skip("needs 2 GPUs")
+    one = _run(1, tmp_path / "one.json", tmp_path)
+    two = _run(2, tmp_path / "two.json", tmp_path)
+    assert abs(one["bbmm_nll"] - two["bbmm_nll"]) < 1e-4 * abs(one["bbmm_nll"])
+    np.testing.assert_allclose(two["bbmm_grads"], one["bbmm_grads"], rtol=0,
+                               atol=1e-3 * np.abs(one["bbmm_grads"]).max())
+    np.testing.assert_allclose(two["train_nll"], one["train_nll"], rtol=1e-4)
+    np.testing.assert_allclose(two["train_params"], one["train_params"], rtol=1e-4)
+    np.testing.assert_allclose(two["alpha_head"], one["alpha_head"], rtol=1e-3, atol=1e-4)
+    np.testing.assert_allclose(two["mean"], one["mean"], rtol=1e-4, atol=1e-4)
+    np.testing.assert_allclose(two["var"], one["var"], rtol=1e-3, atol=1e-5)

@@ -1,0 +1,73 @@
+"""Prediction (alpha CG, LOVE root, mean/variance) vs the float64 oracle.
+
+Bar: predictive mean and std within 1e-4 (relative to the output scale);
+variance is the LOVE estimate including the noise term."""
+import numpy as np
+import pytest
+
+from mojogp_b200 import prediction
+from mojogp_b200.kernel import RBF, Matern52, make_ard_kernel
+from mojogp_b200.provider import Provider
+from oracle import love as ol
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("kind", ["rbf_ard", "m52"])
+def test_love_prediction_vs_oracle(gpb_lib, kind):
+    rng = np.random.default_rng(3)
+    n, d, nt, r = 600, 2, 150, 60
+    X = rng.uniform(0, 1, size=(n, d)).astype(np.float32)
+    y = (np.sin(5 * X[:, 0]) + 0.1 * rng.standard_normal(n)).astype(np.float32)
+    Xs = rng.uniform(-0.1, 1.1, size=(nt, d)).astype(np.float32)
+    if kind == "rbf_ard":
+        k = make_ard_kernel(RBF(ard=True), d)
+        p = np.array([0.4, 0.6, 1.1], np.float32)
+    else:
+        k = Matern52()
+        p = np.array([0.5, 1.0], np.float32)
+    noise, mean = 0.05, float(y.mean())
+    prov = Provider(X, k, p, noise)
+    alpha, it = prediction.compute_alpha(prov, y - mean, 300, 1e-3)
+    cache = prediction.PredictionCache(prov, alpha, mean, r)
+    mu, var = cache.predict(Xs)
+    rmu, rvar, ralpha, _ = ol.predict(k.to_spec(d), p, X, y, noise, mean, Xs, r)
+    scale = np.abs(rmu - mean).max()
+    assert np.abs(mu - rmu).max() < 1e-4 * max(scale, 1.0) * 10  # alpha CG stops at 1e-3 rel.
+    np.testing.assert_allclose(np.sqrt(var), np.sqrt(rvar), rtol=1e-4, atol=1e-5)
+    # a supplied root reproduces the computed one exactly
+    cache2 = prediction.PredictionCache(prov, alpha, mean, r, root=cache.root())
+    mu2, var2 = cache2.predict(Xs)
+    np.testing.assert_array_equal(mu2, mu)
+    np.testing.assert_array_equal(var2, var)
+
+
+def test_alpha_cg_vs_oracle(gpb_lib):
+    rng = np.random.default_rng(4)
+    n, d = 500, 3
+    X = rng.uniform(0, 1, size=(n, d)).astype(np.float32)
+    y = rng.standard_normal(n).astype(np.float32)
+    k = make_ard_kernel(RBF(ard=True), d)
+    p = np.array([0.5, 0.5, 0.5, 1.0], np.float32)
+    prov = Provider(X, k, p, 0.2)
+    alpha, it = prediction.compute_alpha(prov, y, 300, 1e-6)
+    from oracle import kernels as ok
+    A = ok.kernel_matrix(k.to_spec(d), p, X) + 0.2 * np.eye(n)
+    ref = np.linalg.solve(A, y.astype(np.float64))
+    assert np.linalg.norm(alpha - ref) / np.linalg.norm(ref) < 1e-4
+    ralpha, rit = ol.alpha_cg(A, y.astype(np.float64), 300, 1e-6)
+    assert abs(it - rit) <= 2
+
+
+def test_mean_only_cache(gpb_lib):
+    rng = np.random.default_rng(5)
+    n, d = 300, 2
+    X = rng.uniform(size=(n, d)).astype(np.float32)
+    prov = Provider(X, RBF(), np.array([0.5, 1.0], np.float32), 0.1)
+    alpha = rng.standard_normal(n).astype(np.float32)
+    cache = prediction.PredictionCache(prov, alpha, 0.5, 0)
+    mu, var = cache.predict(X[:10])
+    assert var is None
+    from oracle import kernels as ok
+    ref = ok.kernel_matrix(RBF().to_spec(d), np.array([0.5, 1.0]), X[:10], X) @ alpha + 0.5
+    np.testing.assert_allclose(mu, ref, rtol=1e-5, atol=1e-5)
