@@ -39,9 +39,9 @@ def parse():
     ap.add_argument("--steps", type=int, default=5)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--n", type=int, default=1_000_000)
-    ap.add_argument("--d", type=int, default=16)
-    ap.add_argument("--t", type=int, default=16)
+    ap.add_argument("--rows", dest="n", type=int, default=1_000_000)
+    ap.add_argument("--dims", dest="d", type=int, default=16)
+    ap.add_argument("--rhs", dest="t", type=int, default=16)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
     return ap.parse_args()

@@ -37,7 +37,7 @@ def main(out_path):
                       precond_rank=20, init_mean=float(y.mean()), comm=comm)
     res["train_nll"] = tr["nll_history"].tolist()
     res["train_params"] = tr["params"].tolist()
-    alpha, _ = prediction.compute_alpha(prov, yc, 300, 1e-3, comm=comm)
+    alpha, _ = prediction.compute_alpha(prov, yc, 1000, 1e-5, comm=comm)
     res["alpha_head"] = alpha[:50].tolist()
     Xs = rng.uniform(0, 1, size=(200, d)).astype(np.float32)
     cache = prediction.PredictionCache(prov, alpha, float(y.mean()), 40, comm=comm)
