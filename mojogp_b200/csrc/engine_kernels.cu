@@ -108,12 +108,33 @@ int k_scale_cols(float* v, int64_t ld, int64_t nl, int t, const float* scale, in
 __global__ void pack_rows_kernel(const float* __restrict__ xs, int DP, float* __restrict__ v,
                                  int64_t v_ld, int c0, int tcols, int W, int64_t nl,
                                  int64_t nl_pad, float* __restrict__ dst,
-                                 const float* __restrict__ upd_z, const float* __restrict__ upd_beta) {
+                                 const float* __restrict__ upd_z, const float* __restrict__ upd_beta,
+                                 bool dup) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= nl_pad) return;
   float* row = dst + i * W;
   if (i >= nl) {
     for (int k = 0; k < W; ++k) row[k] = 0.f;
+    return;
+  }
+  if (dup) {
+    // paired-row layout: [-x'_k, -x'_k ..., v_c, v_c ...], W = 2 (DP + T)
+    for (int k = 0; k < DP; ++k) row[2 * k] = row[2 * k + 1] = -xs[i * DP + k];
+    const int T = W / 2 - DP;
+    for (int c = 0; c < T; ++c) {
+      float val = 0.f;
+      if (c < tcols) {
+        const int64_t off = (int64_t)(c0 + c) * v_ld + i;
+        val = v[off];
+        if (upd_beta) {
+          const float b = upd_beta[c0 + c];
+          const float zz = upd_z[off];
+          val = (b == 0.f || b != b || val != val) ? zz : fmaf(b, val, zz);
+          v[off] = val;
+        }
+      }
+      row[2 * (DP + c)] = row[2 * (DP + c) + 1] = val;
+    }
     return;
   }
   for (int k = 0; k < DP; ++k) row[k] = xs[i * DP + k];
@@ -134,10 +155,11 @@ __global__ void pack_rows_kernel(const float* __restrict__ xs, int DP, float* __
 }
 int k_pack(const float* xs, int DP, float* v, int64_t v_ld, int c0, int tcols, int T, int64_t nl,
            int64_t nl_pad, float* dst, const float* upd_z, const float* upd_beta,
-           cudaStream_t st) {
+           cudaStream_t st, bool dup) {
   if (nl_pad <= 0) return GPB_OK;
   pack_rows_kernel<<<(unsigned)ceil_div(nl_pad, 256), 256, 0, st>>>(
-      xs, DP, v, v_ld, c0, tcols, packed_width(DP, T), nl, nl_pad, dst, upd_z, upd_beta);
+      xs, DP, v, v_ld, c0, tcols, dup ? 2 * (DP + T) : packed_width(DP, T), nl, nl_pad, dst, upd_z,
+      upd_beta, dup);
   GPB_CHECK_CUDA(cudaGetLastError());
   return GPB_OK;
 }

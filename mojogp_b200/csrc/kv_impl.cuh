@@ -3,16 +3,44 @@
 #pragma once
 
 #include "kv_launch.cuh"
+#include "kv_tiles_x2.cuh"
 
 namespace gpb {
 
+template <int DP, int T, class Ev, bool kX2>
+int kv_launch_impl(const KvLaunch& L);
+
+template <class Ev>
+constexpr int leaf_of() {
+  if constexpr (Ev::kGeneric) {
+    return -1;
+  } else {
+    return Ev::kLeaf;
+  }
+}
+
 template <int DP, int T, class Ev>
 int kv_launch_one(const KvLaunch& L) {
+  if constexpr (!Ev::kGeneric && DP % 2 == 0 && T >= 4) {
+    if (kv_uses_x2(L.eval, DP, T)) return kv_launch_impl<DP, T, Ev, true>(L);
+  }
+  return kv_launch_impl<DP, T, Ev, false>(L);
+}
+
+template <int DP, int T, class Ev, bool kX2>
+int kv_launch_impl(const KvLaunch& L) {
   constexpr bool kGen = Ev::kGeneric;
   constexpr int R = kv_rows_per_thread(DP, T, kGen);
-  constexpr int W = packed_width(DP, T);
-  auto kern = kv_tile_kernel<DP, T, R, kKvBlock, Ev>;
-  const size_t smem = (size_t)kStages * kJT * W * sizeof(float);
+  constexpr int W = kX2 ? packed_width_x2(DP, T) : packed_width(DP, T);
+  constexpr int S = kX2 ? kStagesX2 : kStages;
+  auto kern = [] {
+    if constexpr (kX2) {
+      return kv_tile_x2_kernel<DP, T, R, kKvBlock, leaf_of<Ev>()>;
+    } else {
+      return kv_tile_kernel<DP, T, R, kKvBlock, Ev>;
+    }
+  }();
+  const size_t smem = (size_t)S * kJT * W * sizeof(float);
 
   int dev = 0;
   GPB_CHECK_CUDA(cudaGetDevice(&dev));

@@ -56,6 +56,17 @@ inline int kv_pick_t(int64_t remaining) {
   return 1;
 }
 
+// Paired-row FFMA2 kernel (kv_tiles_x2.cuh) for fast leaves with an even DP
+// and T >= 4; GPB_KV_SCALAR=1 in the environment forces the scalar kernel.
+bool kv_x2_disabled();
+inline bool kv_uses_x2(int eval, int DP, int T) {
+  return eval != kEvalGeneric && DP % 2 == 0 && T >= 4 && !kv_x2_disabled();
+}
+// Floats per packed column row for this launch shape.
+inline int kv_packed_width(int eval, int DP, int T) {
+  return kv_uses_x2(eval, DP, T) ? 2 * (DP + T) : ((DP + T) + 3) / 4 * 4;
+}
+
 // Rows per thread for a (DP, T, generic) instantiation.
 __host__ __device__ constexpr int kv_rows_per_thread(int DP, int T, bool generic) {
   return generic ? 1 : (DP >= 32 ? 2 : 4);

@@ -31,7 +31,8 @@ __host__ __device__ constexpr int packed_width(int DP, int T) { return ((DP + T)
 // TMA ring over a contiguous range of packed column tiles [t0, t0+ntiles).
 // Thread 0 issues 1-D bulk copies; all threads wait on the stage mbarrier
 // with a bounded wait, and a block-wide vote turns a timeout into a clean exit.
-struct TileRing {
+template <int S>
+struct TileRingT {
   float* smem;
   uint64_t* bars;
   const float* src;
@@ -40,12 +41,12 @@ struct TileRing {
 
   __device__ __forceinline__ void start() {
     if (threadIdx.x == 0) {
-      for (int s = 0; s < kStages; ++s) mbar_init(&bars[s], 1);
+      for (int s = 0; s < S; ++s) mbar_init(&bars[s], 1);
       fence_barrier_init();
     }
     __syncthreads();
     if (threadIdx.x == 0) {
-      for (int s = 0; s < kStages && s < ntiles; ++s) issue(s, s);
+      for (int s = 0; s < S && s < ntiles; ++s) issue(s, s);
     }
   }
   __device__ __forceinline__ void issue(int stage, int kt) {
@@ -56,22 +57,23 @@ struct TileRing {
   }
   // Returns the stage buffer, or nullptr (for every thread) on timeout.
   __device__ __forceinline__ const float* acquire(int kt) {
-    const int st = kt % kStages;
-    const bool ok = mbar_wait_bounded(&bars[st], (kt / kStages) & 1);
+    const int st = kt % S;
+    const bool ok = mbar_wait_bounded(&bars[st], (kt / S) & 1);
     if (!__syncthreads_and(ok)) return nullptr;
     return smem + (size_t)st * tile_floats;
   }
   __device__ __forceinline__ void release(int kt) {
     __syncthreads();
-    if (threadIdx.x == 0 && kt + kStages < ntiles) issue(kt % kStages, kt + kStages);
+    if (threadIdx.x == 0 && kt + S < ntiles) issue(kt % S, kt + S);
   }
   __device__ __forceinline__ void fail(int* err) {
     if (threadIdx.x == 0) {
       atomicExch(err, DEV_WAIT_TIMEOUT);
-      for (int s = 0; s < kStages; ++s) (void)mbar_wait_bounded(&bars[s], 0, 100000000ull);
+      for (int s = 0; s < S; ++s) (void)mbar_wait_bounded(&bars[s], 0, 100000000ull);
     }
   }
 };
+using TileRing = TileRingT<kStages>;
 
 // ---------------------------------------------------------------- evaluators
 // Fast single-leaf evaluators work on prescaled inputs x' so that the inner
@@ -91,6 +93,7 @@ template <int LEAF>
 struct FastEval {
   using Params = FastParams;
   static constexpr bool kGeneric = false;
+  static constexpr int kLeaf = LEAF;
   __device__ __forceinline__ static float value(float u, const FastParams& fp) {
     if constexpr (LEAF == GPB_KERNEL_RBF) {
       return ex2_approx(-u);

@@ -3,6 +3,8 @@
 #include "kv_launch.cuh"
 #include "matvec.cuh"
 
+#include <cstdlib>
+
 namespace gpb {
 
 int launch_kv(const KvLaunch& L) {
@@ -101,10 +103,47 @@ __global__ void pack_kernel(const float* __restrict__ xs, int DP, const float* _
   }
 }
 
+// Paired-row layout: every value twice, x' negated (kv_tiles_x2.cuh).
+__global__ void pack_dup_kernel(const float* __restrict__ xs, int DP, const float* __restrict__ v,
+                                int64_t v_ld, int tcols, int T, int64_t n, int64_t npad,
+                                float* __restrict__ xv) {
+  const int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (j >= npad) return;
+  const int W = 2 * (DP + T);
+  float2* row = reinterpret_cast<float2*>(xv + j * W);
+  if (j < n) {
+    for (int k = 0; k < DP; ++k) {
+      const float x = -xs[j * DP + k];
+      row[k] = make_float2(x, x);
+    }
+    for (int c = 0; c < T; ++c) {
+      const float a = (c < tcols) ? v[c * v_ld + j] : 0.f;
+      row[DP + c] = make_float2(a, a);
+    }
+  } else {
+    for (int k = 0; k < DP + T; ++k) row[k] = make_float2(0.f, 0.f);
+  }
+}
+
+bool kv_x2_disabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("GPB_KV_SCALAR");
+    v = (e && e[0] == '1') ? 1 : 0;
+  }
+  return v == 1;
+}
+
 int launch_pack(const float* xs, int DP, const float* v, int64_t v_ld, int tcols, int T, int64_t n,
-                int64_t npad, float* xv, cudaStream_t stream) {
+                int64_t npad, float* xv, cudaStream_t stream, bool dup) {
   const int W = packed_width(DP, T);
   if (npad == 0) return GPB_OK;
+  if (dup) {
+    pack_dup_kernel<<<(unsigned)ceil_div(npad, 256), 256, 0, stream>>>(xs, DP, v, v_ld, tcols, T,
+                                                                      n, npad, xv);
+    GPB_CHECK_CUDA(cudaGetLastError());
+    return GPB_OK;
+  }
   pack_kernel<<<(unsigned)ceil_div(npad, 256), 256, 0, stream>>>(xs, DP, v, v_ld, tcols, n, npad,
                                                                 W, xv);
   GPB_CHECK_CUDA(cudaGetLastError());

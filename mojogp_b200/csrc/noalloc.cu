@@ -57,7 +57,7 @@ extern "C" int gpb_forward_matvec_noalloc(gpb_provider* p, float* out_dev, const
   const int64_t npad = round_up(n, kJT);
   const int Tmax = kv_pick_t(ncols);
   const int64_t xs_floats = round_up(n * DP, 64);
-  const int64_t xv_floats = round_up(npad * packed_width(DP, Tmax), 64);
+  const int64_t xv_floats = round_up(npad * kv_packed_width(p->eval, DP, Tmax), 64);
   const int64_t need = xs_floats + xv_floats;
   GPB_REQUIRE(need <= kNoAllocScratchFloats, GPB_ERR_INVALID,
               "gpb_forward_matvec_noalloc: n=%lld needs %lld scratch floats but the fixed "
@@ -75,7 +75,8 @@ extern "C" int gpb_forward_matvec_noalloc(gpb_provider* p, float* out_dev, const
     const int64_t rem = ncols - c0;
     const int T = kv_pick_t(rem);
     const int tcols = (int)std::min<int64_t>(rem, T);
-    GPB_TRY(launch_pack(xs, DP, v_dev + c0 * n, n, tcols, T, n, npad, xv, st));
+    GPB_TRY(launch_pack(xs, DP, v_dev + c0 * n, n, tcols, T, n, npad, xv, st,
+                        kv_uses_x2(p->eval, DP, T)));
     KvLaunch L{};
     L.eval = p->eval;
     L.DP = DP;
