@@ -1,0 +1,375 @@
+"""SingleOutputGP: the reference's public single-output API on the B200 engine.
+
+Mirrors mojogp/gp.py (SingleOutputGP 245-3949) for the matrix-free route:
+  * fit(X, y, method="matrix_free") with the balanced/fast/accurate presets
+    (gp.py:790-858), the matrix-free preconditioner defaults (1437-1457), the
+    large-n 1-D/low-d RBF initial lengthscale tweak (1376-1408) and
+    init_mean = mean(y) (1576-1578);
+  * predict(X*, return_std / return_var, variance_method="love" | "mean_only")
+    with the prediction solver config of gp.py:85-199 (alpha CG max(...,300)
+    iterations at min(...,1e-3); LOVE rank max(max_tridiag, 100), 200 for ARD);
+  * prepare_prediction_cache, log_marginal_likelihood (= -per-sample NLL,
+    gp.py:3642-3646), get_params, save / load (JSON config + .npz arrays,
+    gp.py:3648-3913).
+Training and prediction run in the CUDA library (engine.py, prediction.py);
+there is no CPU route. Multi-GPU: pass a distributed.Communicator as `comm`.
+"""
+from __future__ import annotations
+
+import json
+from dataclasses import dataclass
+from pathlib import Path
+from typing import Optional
+
+import numpy as np
+
+from . import engine, prediction
+from .kernel import KernelNode, KernelType, make_ard_kernel
+from .provider import Provider
+
+_DEFAULT_PREDICT_LANCZOS_RANK = 100
+_DEFAULT_ARD_PREDICT_LANCZOS_RANK = 200
+_DEFAULT_PREDICT_MAX_CG_ITER = 300
+_DEFAULT_PREDICT_CG_TOL = 1e-3
+
+
+@dataclass
+class TrainingResult:
+    params: np.ndarray
+    noise: float
+    mean: float
+    nll: float
+    iterations: int
+    converged: bool
+    lanczos_root: Optional[np.ndarray] = None
+    lanczos_rank: int = 0
+    nll_history: Optional[np.ndarray] = None
+    cg_iterations_history: Optional[np.ndarray] = None
+    iter_times_ms: Optional[np.ndarray] = None
+
+
+@dataclass
+class PredictionResult:
+    mean: np.ndarray
+    variance: np.ndarray
+    std: np.ndarray
+
+
+class SingleOutputGP:
+    """Exact GP with a composable kernel, trained matrix-free on B200."""
+
+    _PRESETS = {
+        "fast": {"max_cg_iter": 50, "cg_tol": 5e-2, "num_probes": 5, "max_tridiag_iter": 15,
+                 "precond_rank": 50, "precond_rebuild_threshold": 0.75, "precond": "greedy"},
+        "balanced": {"max_cg_iter": 100, "cg_tol": 1e-2, "num_probes": 10, "max_tridiag_iter": 30,
+                     "precond_rank": 100, "precond_rebuild_threshold": 0.5, "precond": "greedy"},
+        "accurate": {"max_cg_iter": 200, "cg_tol": 1e-3, "num_probes": 20, "max_tridiag_iter": 60,
+                     "precond_rank": 200, "precond_rebuild_threshold": 0.25, "precond": "greedy"},
+    }
+
+    def __init__(self, kernel: KernelNode, *, init_mean: Optional[float] = None,
+                 verbose: bool = False, device: int = 0):
+        if not isinstance(kernel, KernelNode):
+            raise TypeError(
+                f"kernel must be a KernelNode instance (e.g. RBF(), Matern52()), got "
+                f"{type(kernel).__name__}")
+        self.kernel_spec = kernel
+        self.kernel: Optional[KernelNode] = None
+        self.ard = kernel.has_ard()
+        self.verbose = verbose
+        self.device = device
+        self._init_mean = init_mean
+        self._X_train = None
+        self._y_train = None
+        self._obs_noise = None
+        self._provider: Optional[Provider] = None
+        self._training_result: Optional[TrainingResult] = None
+        self._train_info: dict = {}
+        self._cache = None
+        self._cache_key = None
+        self._comm = None
+        self.dim = None
+
+    # ----------------------------------------------------------------- helpers
+    @staticmethod
+    def _resolve_cg_params(preset=None, **over) -> dict:
+        base = dict(SingleOutputGP._PRESETS[preset or "balanced"])
+        for k, v in over.items():
+            if v is not None:
+                base[k] = v
+        return base
+
+    def _resolved_kernel(self, dim: int) -> KernelNode:
+        return make_ard_kernel(self.kernel_spec, dim) if self.ard else self.kernel_spec.resolve_ard(dim)
+
+    def _single_type(self, kt: KernelType) -> bool:
+        k = self.kernel_spec
+        return k.is_leaf() and k.kernel_type == kt
+
+    @property
+    def _is_trained(self) -> bool:
+        return self._training_result is not None
+
+    # -------------------------------------------------------------------- fit
+    def fit(self, X, y, max_iterations: int = 100, learning_rate: float = 0.01,
+            initial_noise: float = 0.1, initial_params: Optional[np.ndarray] = None,
+            method: str = "auto", enable_early_stopping: bool = False,
+            early_stop_patience: int = 10, early_stop_tol: float = 1e-4,
+            verbose: Optional[bool] = None, preset: Optional[str] = None,
+            max_cg_iterations: Optional[int] = None, cg_tolerance: Optional[float] = None,
+            num_probes: Optional[int] = None, max_tridiag_iterations: Optional[int] = None,
+            preconditioner_rank: Optional[int] = None,
+            precond_rebuild_threshold: Optional[float] = None,
+            preconditioner: Optional[str] = None, use_preconditioner: Optional[bool] = None,
+            lr_schedule: str = "constant", prepare_prediction_cache: bool = False,
+            prediction_cache_rank: Optional[int] = None,
+            observation_noise: Optional[np.ndarray] = None, learn_noise: bool = True,
+            comm=None) -> TrainingResult:
+        """Train hyperparameters by BBMM (mBCG + SLQ) with Adam on the GPU."""
+        X = np.ascontiguousarray(X, dtype=np.float32)
+        y = np.ascontiguousarray(y, dtype=np.float32)
+        if X.ndim == 1:
+            X = X[:, None]
+        if X.ndim != 2:
+            raise ValueError(f"X must be 2D, got {X.ndim}D")
+        if y.ndim != 1:
+            raise ValueError(f"y must be 1D, got {y.ndim}D")
+        if X.shape[0] != y.shape[0]:
+            raise ValueError(f"X and y have different rows: {X.shape[0]} vs {y.shape[0]}")
+        if X.shape[0] == 0:
+            raise ValueError("cannot fit on an empty dataset")
+        if not (np.all(np.isfinite(X)) and np.all(np.isfinite(y))):
+            raise ValueError("X and y must be finite")
+        if method not in ("auto", "matrix_free"):
+            raise NotImplementedError(
+                f"method={method!r}: this build implements the matrix-free route only")
+        if lr_schedule not in ("constant", "cosine"):
+            raise ValueError("lr_schedule must be 'constant' or 'cosine'")
+        n, dim = X.shape
+        self.dim = dim
+        self._comm = comm
+        self.kernel = self._resolved_kernel(dim)
+        P = self.kernel.num_params()
+        default_params = initial_params is None
+        params = (self.kernel.get_initial_params() if default_params
+                  else np.asarray(initial_params, np.float32).ravel())
+        if params.shape[0] != P:
+            raise ValueError(f"initial_params must have {P} entries, got {params.shape[0]}")
+        params = params.astype(np.float32).copy()
+        # gp.py:1376-1408: milder lengthscale start for large low-d matrix-free RBF
+        if (default_params and learning_rate <= 0.05 and self._single_type(KernelType.RBF)
+                and not self.ard and 1 < dim <= 8 and n >= 10000):
+            params[0] = min(float(params[0]), 0.6)
+        # gp.py:1437-1457: matrix-free preconditioner defaults
+        explicit = (preconditioner is not None or preconditioner_rank is not None
+                    or use_preconditioner is not None)
+        rank = preconditioner_rank
+        if not explicit:
+            if self._single_type(KernelType.RBF) and not self.ard and 1 < dim <= 8 and n >= 5000:
+                preconditioner, rank = "greedy", 256
+            else:
+                rank = 0
+        if preconditioner not in (None, "greedy"):
+            raise NotImplementedError(
+                f"preconditioner={preconditioner!r}: only the greedy pivoted Cholesky is built")
+        cg = self._resolve_cg_params(preset, max_cg_iter=max_cg_iterations, cg_tol=cg_tolerance,
+                                     num_probes=num_probes,
+                                     max_tridiag_iter=max_tridiag_iterations,
+                                     precond_rank=rank,
+                                     precond_rebuild_threshold=precond_rebuild_threshold)
+        use_p = bool(use_preconditioner) if use_preconditioner is not None else cg["precond_rank"] > 0
+        if observation_noise is not None:
+            use_p = False  # the Woodbury preconditioner assumes scalar noise
+        init_mean = float(np.mean(y)) if self._init_mean is None else float(self._init_mean)
+        self._destroy()
+        self._X_train, self._y_train = X, y
+        self._obs_noise = None if observation_noise is None else np.asarray(observation_noise, np.float32)
+        self._provider = Provider(X, self.kernel, params, initial_noise, device=self.device,
+                                  noise_vector=self._obs_noise)
+        res = engine.train(
+            self._provider, y, max_iterations=max_iterations, learning_rate=learning_rate,
+            num_probes=cg["num_probes"], max_cg_iter=cg["max_cg_iter"], cg_tol=cg["cg_tol"],
+            precond_rank=cg["precond_rank"] if use_p else 0,
+            max_tridiag_iter=cg["max_tridiag_iter"],
+            precond_rebuild_threshold=cg["precond_rebuild_threshold"],
+            use_cosine_lr=lr_schedule == "cosine", use_preconditioner=use_p,
+            learn_noise=learn_noise, init_mean=init_mean,
+            enable_early_stopping=enable_early_stopping, early_stop_patience=early_stop_patience,
+            early_stop_tol=early_stop_tol,
+            verbose=self.verbose if verbose is None else verbose,
+            trainable_mask=self.kernel.engine_trainable_mask(), comm=comm)
+        self._train_info = {"max_cg_iterations": cg["max_cg_iter"], "cg_tolerance": cg["cg_tol"],
+                            "max_tridiag_iter": cg["max_tridiag_iter"],
+                            "precond_rank": res["precond_rank"],
+                            "precond_build_count": res["precond_build_count"],
+                            "precond_build_time_ms": res["precond_build_time_ms"]}
+        self._training_result = TrainingResult(
+            params=res["params"], noise=res["noise"], mean=res["mean"], nll=res["final_nll"],
+            iterations=res["iterations"], converged=res["converged"],
+            lanczos_rank=cg["max_tridiag_iter"], nll_history=res["nll_history"],
+            cg_iterations_history=res["cg_iterations_history"],
+            iter_times_ms=res["iter_times_ms"])
+        if prepare_prediction_cache:
+            self.prepare_prediction_cache(max_root_decomposition_size=prediction_cache_rank)
+        return self._training_result
+
+    # ---------------------------------------------------------------- predict
+    def _solver_config(self, max_cg_iterations=None, cg_tolerance=None,
+                       max_root_decomposition_size=None) -> dict:
+        ti = self._train_info
+        rank = max(int(self._training_result.lanczos_rank), _DEFAULT_PREDICT_LANCZOS_RANK)
+        if self.ard:
+            rank = max(rank, _DEFAULT_ARD_PREDICT_LANCZOS_RANK)
+        if max_root_decomposition_size is not None:
+            rank = int(max_root_decomposition_size)
+        rank = min(rank, self._X_train.shape[0])
+        return {
+            "max_cg_iterations": int(max_cg_iterations if max_cg_iterations is not None else
+                                     max(ti.get("max_cg_iterations", 0), _DEFAULT_PREDICT_MAX_CG_ITER)),
+            "cg_tolerance": float(cg_tolerance if cg_tolerance is not None else
+                                  min(ti.get("cg_tolerance", 1.0), _DEFAULT_PREDICT_CG_TOL)),
+            "max_root_decomposition_size": rank,
+        }
+
+    def prepare_prediction_cache(self, variance_method: str = "love",
+                                 max_root_decomposition_size: Optional[int] = None,
+                                 max_cg_iterations: Optional[int] = None,
+                                 cg_tolerance: Optional[float] = None):
+        if not self._is_trained:
+            raise RuntimeError("GP must be trained first.")
+        cfg = self._solver_config(max_cg_iterations, cg_tolerance, max_root_decomposition_size)
+        rank = cfg["max_root_decomposition_size"] if variance_method == "love" else 0
+        key = (cfg["max_cg_iterations"], cfg["cg_tolerance"], rank)
+        if self._cache is not None and self._cache_key == key:
+            return self._cache
+        tr = self._training_result
+        alpha, _ = prediction.compute_alpha(self._provider, self._y_train - tr.mean,
+                                            cfg["max_cg_iterations"], cfg["cg_tolerance"],
+                                            comm=self._comm)
+        root = tr.lanczos_root if (tr.lanczos_root is not None and rank > 0 and
+                                   tr.lanczos_root.shape == (rank, self._X_train.shape[0])) else None
+        self._cache = prediction.PredictionCache(self._provider, alpha, tr.mean, rank, root=root,
+                                                 comm=self._comm)
+        if rank > 0 and root is None:
+            tr.lanczos_root = self._cache.root()
+        self._cache_key = key
+        self._alpha = alpha
+        return self._cache
+
+    def predict(self, X_test, return_std: bool = False, return_var: bool = False,
+                variance_method: str = "love", max_cg_iterations: Optional[int] = None,
+                cg_tolerance: Optional[float] = None,
+                max_root_decomposition_size: Optional[int] = None):
+        """Predictive mean (and LOVE variance / std, including the noise term)."""
+        if not self._is_trained:
+            raise RuntimeError("GP must be trained first.")
+        if variance_method not in ("love", "mean_only"):
+            raise NotImplementedError(
+                f"variance_method={variance_method!r}: this build implements 'love' and 'mean_only'")
+        Xt = np.ascontiguousarray(X_test, dtype=np.float32)
+        if Xt.ndim == 1:
+            Xt = Xt[:, None]
+        if Xt.shape[1] != self.dim:
+            raise ValueError(f"X_test has {Xt.shape[1]} features, expected {self.dim}")
+        want_var = variance_method == "love"
+        cache = self.prepare_prediction_cache("love" if want_var else "mean_only",
+                                              max_root_decomposition_size, max_cg_iterations,
+                                              cg_tolerance)
+        mean, var = cache.predict(Xt, return_var=want_var)
+        if var is None:
+            var = np.zeros_like(mean)
+        std = np.sqrt(np.maximum(var, 0))
+        if return_var:
+            return mean, var
+        if return_std:
+            return mean, std
+        return PredictionResult(mean=mean, variance=var, std=std)
+
+    # ---------------------------------------------------------------- queries
+    def log_marginal_likelihood(self) -> float:
+        if not self._is_trained:
+            raise RuntimeError("GP must be trained first.")
+        return -float(self._training_result.nll)
+
+    def get_params(self) -> dict:
+        if not self._is_trained:
+            raise RuntimeError("GP must be trained first.")
+        tr = self._training_result
+        out = dict(zip(self.kernel.get_param_names(), map(float, tr.params)))
+        out["noise"] = float(tr.noise)
+        out["mean"] = float(tr.mean)
+        return out
+
+    @property
+    def noise(self) -> float:
+        return float(self._training_result.noise)
+
+    @property
+    def mean(self) -> float:
+        return float(self._training_result.mean)
+
+    # -------------------------------------------------------------- persist
+    def save(self, path: str) -> None:
+        """JSON config + .npz arrays (training data, params, LOVE root)."""
+        if not self._is_trained:
+            raise RuntimeError("GP must be trained first.")
+        p = Path(path)
+        tr = self._training_result
+        cfg = {"format": "mojogp_b200/1", "kernel": self.kernel_spec.to_dict(), "ard": self.ard,
+               "dim": self.dim, "noise": float(tr.noise), "mean": float(tr.mean),
+               "nll": float(tr.nll), "iterations": int(tr.iterations),
+               "converged": bool(tr.converged), "lanczos_rank": int(tr.lanczos_rank),
+               "train_info": self._train_info}
+        arrays = {"X": self._X_train, "y": self._y_train, "params": tr.params}
+        if tr.lanczos_root is not None:
+            arrays["lanczos_root"] = tr.lanczos_root
+        if tr.nll_history is not None:
+            arrays["nll_history"] = tr.nll_history
+        if self._obs_noise is not None:
+            arrays["observation_noise"] = self._obs_noise
+        p.with_suffix(".json").write_text(json.dumps(cfg, indent=1))
+        np.savez_compressed(p.with_suffix(".npz"), **arrays)
+
+    @classmethod
+    def load(cls, path: str, device: int = 0) -> "SingleOutputGP":
+        p = Path(path)
+        cfg = json.loads(p.with_suffix(".json").read_text())
+        arr = np.load(p.with_suffix(".npz"))
+        gp = cls(KernelNode.from_dict(cfg["kernel"]), device=device)
+        gp.dim = cfg["dim"]
+        gp.kernel = gp._resolved_kernel(gp.dim)
+        gp._X_train, gp._y_train = arr["X"], arr["y"]
+        gp._obs_noise = arr["observation_noise"] if "observation_noise" in arr else None
+        gp._train_info = cfg.get("train_info", {})
+        gp._training_result = TrainingResult(
+            params=arr["params"], noise=cfg["noise"], mean=cfg["mean"], nll=cfg["nll"],
+            iterations=cfg["iterations"], converged=cfg["converged"],
+            lanczos_root=arr["lanczos_root"] if "lanczos_root" in arr else None,
+            lanczos_rank=cfg["lanczos_rank"],
+            nll_history=arr["nll_history"] if "nll_history" in arr else None)
+        gp._provider = Provider(gp._X_train, gp.kernel, arr["params"], cfg["noise"],
+                                device=device, noise_vector=gp._obs_noise)
+        return gp
+
+    def _destroy(self) -> None:
+        if self._cache is not None:
+            self._cache.destroy()
+        self._cache = None
+        self._cache_key = None
+        if self._provider is not None:
+            self._provider.destroy()
+        self._provider = None
+        self._training_result = None
+
+    def __del__(self):
+        try:
+            self._destroy()
+        except Exception:
+            pass
+
+
+def fit_gp(X, y, kernel: KernelNode, **kw) -> SingleOutputGP:
+    """Convenience: construct and fit a SingleOutputGP."""
+    gp = SingleOutputGP(kernel)
+    gp.fit(X, y, **kw)
+    return gp

@@ -1,0 +1,74 @@
+"""SingleOutputGP end to end on config 1 (README hello world: n=2000 1-D RBF,
+50 matrix-free iterations, LOVE prediction at 128 points).
+
+Acceptance floors follow the reference's own integration tests
+(tests/integration/test_exactgp_variance_accuracy.py:48-137): predictions
+from the learned hyperparameters track the exact closed-form posterior
+(mean RMSE < 2e-2, variance RMSE < 1e-2)."""
+import numpy as np
+import pytest
+
+from mojogp_b200 import synthetic
+from mojogp_b200.gp import SingleOutputGP
+from mojogp_b200.kernel import RBF, Matern52
+from oracle import kernels as ok
+
+pytestmark = pytest.mark.gpu
+
+
+def _exact(gp, X, y, Xs):
+    spec = gp.kernel.to_spec(X.shape[1])
+    tr = gp._training_result
+    K = ok.kernel_matrix(spec, tr.params, X) + tr.noise * np.eye(len(X))
+    Ks = ok.kernel_matrix(spec, tr.params, Xs, X)
+    a = np.linalg.solve(K, y - tr.mean)
+    mu = Ks @ a + tr.mean
+    var = np.diag(ok.kernel_matrix(spec, tr.params, Xs)) - np.sum(Ks * np.linalg.solve(K, Ks.T).T, 1)
+    return mu, var + tr.noise
+
+
+def test_config1_fit_predict(gpb_lib, tmp_path):
+    X, y, Xs = synthetic.config1()
+    gp = SingleOutputGP(RBF())
+    tr = gp.fit(X, y, max_iterations=50, method="matrix_free")
+    assert tr.iterations == 50
+    assert np.all(np.isfinite(tr.nll_history))
+    assert tr.nll_history[-1] < tr.nll_history[0]
+    mean, std = gp.predict(Xs, return_std=True)
+    assert mean.shape == (128,) and np.all(std > 0)
+    mu, var = _exact(gp, X.astype(np.float64), y.astype(np.float64), Xs.astype(np.float64))
+    assert np.sqrt(np.mean((mean - mu) ** 2)) < 2e-2
+    assert np.sqrt(np.mean((std ** 2 - var) ** 2)) < 1e-2
+    assert abs(gp.log_marginal_likelihood() + tr.nll) < 1e-6
+    # in-sample fit quality on the noiseless signal
+    m_in = gp.predict(X, variance_method="mean_only").mean
+    assert np.sqrt(np.mean((m_in - np.sin(2 * X[:, 0])) ** 2)) < 0.05
+    # save / load round trip reproduces predictions
+    gp.save(str(tmp_path / "model"))
+    gp2 = SingleOutputGP.load(str(tmp_path / "model"))
+    m2, s2 = gp2.predict(Xs, return_std=True)
+    np.testing.assert_allclose(m2, mean, rtol=1e-5, atol=1e-5)
+    np.testing.assert_allclose(s2, std, rtol=1e-5, atol=1e-6)
+
+
+def test_ard_matern_with_preconditioner(gpb_lib):
+    X, y = synthetic.config2(n=6000, d=4)
+    gp = SingleOutputGP(Matern52(ard=True))
+    tr = gp.fit(X, y, max_iterations=10, learning_rate=0.05, num_probes=15,
+                preconditioner="greedy", preconditioner_rank=50)
+    assert np.all(np.isfinite(tr.nll_history)) and tr.nll_history[-1] < tr.nll_history[0]
+    assert gp._train_info["precond_rank"] == 50
+    p = gp.predict(X[:100])
+    assert np.all(np.isfinite(p.mean)) and np.all(p.variance > 0)
+
+
+def test_input_validation(gpb_lib):
+    gp = SingleOutputGP(RBF())
+    with pytest.raises(ValueError):
+        gp.fit(np.zeros((5, 2)), np.zeros(4))
+    with pytest.raises(ValueError):
+        gp.fit(np.zeros((5, 2)), np.zeros((5, 1)))
+    with pytest.raises(NotImplementedError):
+        gp.fit(np.zeros((5, 2)), np.zeros(5), method="materialized")
+    with pytest.raises(RuntimeError):
+        gp.predict(np.zeros((3, 2)))
