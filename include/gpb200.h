@@ -294,7 +294,8 @@ int gpb_prediction_cache_destroy(gpb_prediction_cache* c);
  * not allocate while they run (an external memory pool or arena, or code where
  * an allocation's implicit synchronisation is not allowed). No counterpart in
  * the reference. Limit: n * DP + round_up(n, 128) * W floats must fit in
- * 8 Mi floats (DP = padded input dims, W = DP + 16 rounded to 4); larger n is
+ * 8 Mi floats (DP = padded input dims, W = packed row width, 2 * (DP + 16)
+ * for 16 right-hand sides: about 100k rows at d = 16); larger n is
  * rejected with GPB_ERR_INVALID. The first call on a device looks up the
  * array's device address, so make that first call before any stream capture.
  * Calls share the array: calls that overlap on the GPU race and must be
