@@ -288,6 +288,34 @@ int gpb_predict_with_cache(gpb_prediction_cache* c, const float* xtest_host, int
                            float* mean_out, float* var_out);
 int gpb_prediction_cache_destroy(gpb_prediction_cache* c);
 
+/* ------------------------------------------------------------------ LMC
+ * Linear model of coregionalisation over R latent providers (same X, n, device):
+ * K_full = sum_s (A_s (x) K_s) + diag(noise_t (x) 1_n) on task-blocked vectors
+ * (element (t, i) at t*n + i). Replaces JITLMCGradientAdapter
+ * (jit_lmc.mojo:131-540) and the LMC kernels (lmc_provider.mojo:45-267).
+ * Latent providers contribute K_s without their own noise. */
+typedef struct gpb_lmc gpb_lmc;
+int gpb_lmc_create(gpb_provider* const* providers, int32_t num_latents, int32_t num_tasks,
+                   gpb_lmc** out);
+int gpb_lmc_destroy(gpb_lmc* h);
+/* A [R][T][T] (symmetric PSD coregionalisation matrices), noise [T]. */
+int gpb_lmc_set_coregion(gpb_lmc* h, const float* A, const float* noise);
+/* out = K_full v for ncols task-blocked columns [ncols][T][n] (device). */
+int gpb_lmc_matvec(gpb_lmc* h, float* out_dev, const float* v_dev, int64_t ncols);
+/* One BBMM evaluation on the LMC operator (combined_inv_quad_logdet.mojo:452
+ * with jit_lmc.mojo:582-691 gradients): NLL per nT, gradients w.r.t. every
+ * latent's kernel params (concatenated), A_s [R][T][T], per-task noise [T],
+ * per-task sum(alpha) [T]; alpha_out [T*n] optional. recycle != 0 warm-starts
+ * from the previous call's solution. */
+int gpb_lmc_bbmm(gpb_lmc* h, const float* y_centered_host, int32_t num_probes, int32_t max_cg_iter,
+                 int32_t max_tridiag_iter, float cg_tol, int32_t iteration, int32_t recycle,
+                 double* nll_out, double* kernel_grads_out, double* grad_A_out,
+                 double* grad_noise_out, double* sum_alpha_out, float* alpha_out,
+                 int32_t* cg_iters_out);
+/* K_full^{-1} rhs by CG (relative-residual stop), rhs and x [T*n] host. */
+int gpb_lmc_solve(gpb_lmc* h, const float* rhs_host, int32_t max_cg_iter, float cg_tol,
+                  float* x_host_out, int32_t* iters_out);
+
 /* Same result as gpb_forward_matvec, but the call allocates no device memory:
  * all scratch lives in one fixed 32 MiB array compiled into the library, held
  * on every GPU that uses it until the process exits. For callers that must

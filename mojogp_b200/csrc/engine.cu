@@ -104,6 +104,12 @@ int Engine::coldots(int npairs, const float* const* a, const float* const* b, in
 
 int Engine::matvec(float* v_local, int64_t v_ld, int t, float* out, int64_t out_ld,
                    const float* update_z, const float* update_beta) {
+  if (op) {
+    GPB_REQUIRE(dist.world == 1 && v_ld == nl && out_ld == nl, GPB_ERR_UNSUPPORTED,
+                "operator matvec needs a single GPU and dense column blocks");
+    if (update_beta) GPB_TRY(k_update_p(v_local, update_z, update_beta, nl, v_ld, t, st));
+    return op->apply(v_local, v_ld, t, out, st);
+  }
   GPB_TRY(provider_refresh_xs(p));
   const int world = dist.world;
   const int64_t rows_total = (int64_t)world * nl_pad;

@@ -47,8 +47,17 @@ struct Reducer {
   int ensure(int max_blocks, int k);
 };
 
+// Linear operator other than a single provider's K + noise (the LMC sum of
+// Kronecker products); when set, Engine::matvec delegates to it.
+struct LinOp {
+  virtual ~LinOp() = default;
+  // out = A v for [t][ld] blocks over all rows (single GPU).
+  virtual int apply(const float* v, int64_t ld, int t, float* out, cudaStream_t st) = 0;
+};
+
 struct Engine {
   gpb_provider* p = nullptr;
+  LinOp* op = nullptr;
   Dist dist;
   cudaStream_t st = nullptr;
   int64_t n = 0, r0 = 0, r1 = 0, nl = 0, nl_pad = 0;
@@ -93,6 +102,9 @@ int k_cg_update(const float* alpha, const float* p, const float* Ap, float* x, f
                 int64_t nl, int64_t ld, int t, cudaStream_t st);
 int k_sub(float* r, const float* a, int64_t count, cudaStream_t st);
 int k_set_rz(float* rz, const double* sums, int t, cudaStream_t st);
+// p = z + beta p with the reference's freeze rules (in place), [t][ld].
+int k_update_p(float* p, const float* z, const float* beta, int64_t nl, int64_t ld, int t,
+               cudaStream_t st);
 
 // Preconditioner kernels.
 int k_ltv(const float* L, int64_t nl, int rank, const float* v, int64_t ld, int t, Reducer& red,

@@ -304,6 +304,24 @@ int k_set_rz(float* rz, const double* sums, int t, cudaStream_t st) {
   return GPB_OK;
 }
 
+__global__ void update_p_kernel(float* p, const float* z, const float* beta, int64_t nl,
+                                int64_t ld, int t) {
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= (int64_t)t * nl) return;
+  const int c = (int)(idx / nl);
+  const int64_t off = c * ld + (idx - (int64_t)c * nl);
+  const float b = beta[c], pv = p[off], zz = z[off];
+  p[off] = (b == 0.f || b != b || pv != pv) ? zz : fmaf(b, pv, zz);
+}
+int k_update_p(float* p, const float* z, const float* beta, int64_t nl, int64_t ld, int t,
+               cudaStream_t st) {
+  const int64_t total = (int64_t)t * nl;
+  if (total <= 0) return GPB_OK;
+  update_p_kernel<<<(unsigned)ceil_div(total, 256), 256, 0, st>>>(p, z, beta, nl, ld, t);
+  GPB_CHECK_CUDA(cudaGetLastError());
+  return GPB_OK;
+}
+
 // x += alpha p; r -= alpha Ap, frozen where alpha is 0/NaN or p/Ap is NaN
 // (cg_solver.mojo:138-178).
 __global__ void cg_update_kernel(const float* __restrict__ alpha, const float* __restrict__ p,

@@ -135,7 +135,7 @@ __global__ void __launch_bounds__(128) bilinear_fast_kernel(
 #pragma unroll
   for (int q = 0; q < NACC; ++q) accd[q] = acct[q] = 0.f;
 
-  const int cstart = has_data ? 1 : 0;
+  const int nd = has_data;  // leading data columns in this chunk
   for (int kt = 0; kt < ntiles; ++kt) {
     const float* buf = ring.acquire(kt);
     if (buf == nullptr) {
@@ -162,11 +162,14 @@ __global__ void __launch_bounds__(128) bilinear_fast_kernel(
         }
         float kap, phi, h;
         fast_value_and_phi<LEAF>(u, fp, kap, phi, h);
-        const float wd = has_data ? ai[r][0] * bj[0] : 0.f;
-        float wt = 0.f;
+        float wd = 0.f, wt = 0.f;
 #pragma unroll
-        for (int c = 0; c < T; ++c)
-          if (c >= cstart) wt = fmaf(ai[r][c], bj[c], wt);
+        for (int c = 0; c < T; ++c) {
+          if (c < nd)
+            wd = fmaf(ai[r][c], bj[c], wd);
+          else
+            wt = fmaf(ai[r][c], bj[c], wt);
+        }
         const float pd = phi * wd, pt = phi * wt;
 #pragma unroll
         for (int k = 0; k < DP; ++k) {
@@ -220,7 +223,7 @@ __global__ void __launch_bounds__(128) bilinear_generic_kernel(
   for (int c = 0; c < T; ++c) ai[c] = (ok && c < tcols) ? a[c * a_ld + i] : 0.f;
   float gd[GPB_MAX_PARAMS], gt[GPB_MAX_PARAMS], g[GPB_MAX_PARAMS];
   for (int q = 0; q < P; ++q) gd[q] = gt[q] = 0.f;
-  const int cstart = has_data ? 1 : 0;
+  const int nd = has_data;
   for (int kt = 0; kt < ntiles; ++kt) {
     const float* buf = ring.acquire(kt);
     if (buf == nullptr) {
@@ -231,9 +234,13 @@ __global__ void __launch_bounds__(128) bilinear_generic_kernel(
       const float* rowp = buf + j * W;
       float xj[DP];
       for (int k = 0; k < DP; ++k) xj[k] = rowp[k];
-      const float wd = has_data ? ai[0] * rowp[DP] : 0.f;
-      float wt = 0.f;
-      for (int c = cstart; c < T; ++c) wt = fmaf(ai[c], rowp[DP + c], wt);
+      float wd = 0.f, wt = 0.f;
+      for (int c = 0; c < T; ++c) {
+        if (c < nd)
+          wd = fmaf(ai[c], rowp[DP + c], wd);
+        else
+          wt = fmaf(ai[c], rowp[DP + c], wt);
+      }
       tree_eval<true>(K, xi, xj, g);
       for (int q = 0; q < P; ++q) {
         gd[q] = fmaf(g[q], wd, gd[q]);
@@ -389,6 +396,13 @@ int bilinear_generic_dp(int DP, int T, const float* xrow, const float* a, int64_
 int provider_bilinear_rows(gpb_provider* p, const float* a_dev, int64_t a_ld, const float* b_dev,
                            int64_t ncols, int64_t row_begin, int64_t row_end, double* data_out,
                            double* trace_out, cudaStream_t st) {
+  return provider_bilinear_rows_nd(p, a_dev, a_ld, b_dev, ncols, row_begin, row_end, 1, data_out,
+                                   trace_out, st);
+}
+
+int provider_bilinear_rows_nd(gpb_provider* p, const float* a_dev, int64_t a_ld, const float* b_dev,
+                              int64_t ncols, int64_t row_begin, int64_t row_end, int64_t ndata,
+                              double* data_out, double* trace_out, cudaStream_t st) {
   const int P = p->dk.nparams;
   for (int q = 0; q < P; ++q) data_out[q] = trace_out[q] = 0.0;
   const int64_t nrow = row_end - row_begin;
@@ -414,7 +428,8 @@ int provider_bilinear_rows(gpb_provider* p, const float* a_dev, int64_t a_ld, co
     void* part = nullptr;
     GPB_TRY(p->ws.get(WS_GRAD, (size_t)cap * sizeof(float) + 4096, &part));
     int64_t nb = 0;
-    const int has_data = c0 == 0 ? 1 : 0;
+    // number of leading data columns inside this 16-column chunk
+    const int has_data = (int)std::max<int64_t>(0, std::min<int64_t>(ndata - c0, tcols));
     const float* a_chunk = a_dev + c0 * a_ld;  // a_dev points at row_begin
     int s;
     switch (p->eval) {

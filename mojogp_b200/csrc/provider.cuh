@@ -83,5 +83,10 @@ int provider_prescale_rows(gpb_provider* p, const float* x_raw, int64_t nrow, in
 int provider_bilinear_rows(gpb_provider* p, const float* a_dev, int64_t a_ld, const float* b_dev,
                            int64_t ncols, int64_t row_begin, int64_t row_end, double* data_out,
                            double* trace_out, cudaStream_t st);
+// Same with the first `ndata` columns as data columns (the rest are trace
+// columns): data_out = sum_{c<ndata} a_c' dK b_c, trace_out over c >= ndata.
+int provider_bilinear_rows_nd(gpb_provider* p, const float* a_dev, int64_t a_ld, const float* b_dev,
+                              int64_t ncols, int64_t row_begin, int64_t row_end, int64_t ndata,
+                              double* data_out, double* trace_out, cudaStream_t st);
 
 }  // namespace gpb

@@ -264,6 +264,7 @@ int bbmm_step(Engine& E, Precond* P, BBMMState& S, int num_probes, int max_cg, i
   // 6. Gradients: a = [alpha | u_j * |z_j|], b = [alpha | P^{-1} z_j].
   float* A = sol;  // probe columns scaled by probe norms in place
   GPB_TRY(k_scale_cols(A + nl, nl, nl, num_probes, pnorms_dev, 0, st));
+  if (E.op) return lmc_bbmm_gradients(E, S, A, sampled, num_probes, R);
   float* B = S.rf.f();
   GPB_TRY(k_copy(B, sol, nl, st));
   if (use_p)

@@ -25,6 +25,8 @@ struct BBMMResult {
   double nll = 0, inv_quad = 0, logdet = 0, sum_alpha = 0;
   std::vector<double> grads;  // P kernel params + noise
   int cg_iters = 0;
+  // LMC extras: dNLL/dA_s [R][T][T], per-task noise gradients, per-task sum(alpha)
+  std::vector<double> grad_A, grad_noise_task, sum_alpha_task;
 };
 
 int cg_solve(Engine& E, Precond* P, BBMMState& S, const float* rhs, int t, int max_iter,
@@ -32,5 +34,11 @@ int cg_solve(Engine& E, Precond* P, BBMMState& S, const float* rhs, int t, int m
 int bbmm_step(Engine& E, Precond* P, BBMMState& S, int num_probes, int max_cg, int max_tridiag,
               float tol, int iteration, bool recycle, BBMMResult& R);
 int k_sub_scalar(float* v, int64_t count, float s, cudaStream_t st);
+// (K + noise) x = y by CG with the relative-residual stop (predict.cu).
+int alpha_cg(Engine& E, const float* y_local, float* x, int max_iter, float tol, int* iters_out);
+// LMC gradients from the BBMM solution (lmc.cu); sol holds [alpha | scaled
+// probe solutions], sampled the unnormalised probes.
+int lmc_bbmm_gradients(Engine& E, BBMMState& S, float* sol, const float* sampled, int num_probes,
+                       BBMMResult& R);
 
 }  // namespace gpb

@@ -1,0 +1,273 @@
+"""MultiOutputLMCGP: linear model of coregionalisation, matrix-free on B200.
+
+Mirrors the reference's MultiOutputLMCGP (mojogp/multi_output_gp.py:3465-5835)
+for the matrix-free route and its training loop train_lmc_jit
+(mojogp/kernels/jit/jit_lmc.mojo:699-1529): per-latent kernels K_s sharing X,
+coregionalisation A_s = L_s L_s^T + diag(v_s) with softplus diagonals, per-task
+noise and per-task constant means, Adam with gradient clip 10, NLL per n*T.
+The LMC preconditioner (lmc_preconditioner.mojo) is not built: training runs
+unpreconditioned mBCG.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import math
+from typing import List, Optional
+
+import numpy as np
+
+from . import _lib
+from .kernel import Kernel, KernelNode, make_ard_kernel
+from .provider import Provider
+
+_STR = {"rbf": Kernel.rbf, "matern12": Kernel.matern12, "matern32": Kernel.matern32,
+        "matern52": Kernel.matern52, "periodic": Kernel.periodic, "rq": Kernel.rq,
+        "linear": Kernel.linear, "polynomial": Kernel.polynomial}
+
+
+def _sp(x):
+    return float(np.where(x > 20, x, np.log1p(np.exp(np.minimum(x, 20)))))
+
+
+def _isp(y):
+    return y if y > 20 else (math.log(y) if y < 1e-6 else math.log(math.expm1(y)))
+
+
+def _dsp(x):
+    return 1.0 / (1.0 + math.exp(-x)) if x > -20 else math.exp(x)
+
+
+class LMC:
+    """Thin owner of a gpb_lmc handle over R providers."""
+
+    def __init__(self, providers: List[Provider], num_tasks: int):
+        self.providers = providers
+        self.T = num_tasks
+        self.R = len(providers)
+        self.n = providers[0].n
+        arr = (C.c_void_p * self.R)(*[p.handle for p in providers])
+        h = C.c_void_p()
+        _lib.call("gpb_lmc_create", C.cast(arr, C.c_void_p), self.R, num_tasks, C.byref(h))
+        self.handle = h.value
+
+    def set_coregion(self, A: np.ndarray, noise: np.ndarray) -> None:
+        A = np.ascontiguousarray(A, np.float32)
+        nz = np.ascontiguousarray(noise, np.float32)
+        _lib.call("gpb_lmc_set_coregion", C.c_void_p(self.handle), C.c_void_p(A.ctypes.data),
+                  C.c_void_p(nz.ctypes.data))
+
+    def bbmm(self, y_blocked: np.ndarray, num_probes: int, max_cg: int, max_tridiag: int,
+             tol: float, iteration: int, recycle: bool):
+        y = np.ascontiguousarray(y_blocked, np.float32).ravel()
+        nll = C.c_double()
+        P = sum(p.num_params for p in self.providers)
+        kg = np.zeros(P)
+        gA = np.zeros((self.R, self.T, self.T))
+        gn = np.zeros(self.T)
+        sa = np.zeros(self.T)
+        alpha = np.zeros(self.n * self.T, np.float32)
+        it = C.c_int32()
+        _lib.call("gpb_lmc_bbmm", C.c_void_p(self.handle), C.c_void_p(y.ctypes.data), num_probes,
+                  max_cg, max_tridiag, float(tol), iteration, int(recycle), C.byref(nll),
+                  C.c_void_p(kg.ctypes.data), C.c_void_p(gA.ctypes.data),
+                  C.c_void_p(gn.ctypes.data), C.c_void_p(sa.ctypes.data),
+                  C.c_void_p(alpha.ctypes.data), C.byref(it))
+        return {"nll": nll.value, "kgrads": kg, "gA": gA, "gnoise": gn, "sum_alpha": sa,
+                "alpha": alpha, "cg_iters": it.value}
+
+    def solve(self, rhs: np.ndarray, max_cg: int = 300, tol: float = 1e-3):
+        r = np.ascontiguousarray(rhs, np.float32).ravel()
+        x = np.zeros_like(r)
+        it = C.c_int32()
+        _lib.call("gpb_lmc_solve", C.c_void_p(self.handle), C.c_void_p(r.ctypes.data), max_cg,
+                  float(tol), C.c_void_p(x.ctypes.data), C.byref(it))
+        return x, it.value
+
+    def destroy(self) -> None:
+        if getattr(self, "handle", None):
+            _lib.lib().gpb_lmc_destroy(C.c_void_p(self.handle))
+            self.handle = None
+
+    def __del__(self):
+        try:
+            self.destroy()
+        except Exception:
+            pass
+
+
+class MultiOutputLMCGP:
+    """LMC multi-output GP with heterogeneous latent kernels."""
+
+    def __init__(self, kernels: list, num_probes: int = 10, max_cg_iterations: int = 200,
+                 cg_tolerance: float = 1.0, max_tridiag_iterations: int = 30, ard: bool = False,
+                 init_mean=None, device: int = 0):
+        ks = []
+        for k in kernels:
+            if isinstance(k, str):
+                if k.lower() not in _STR:
+                    raise ValueError(f"Unknown kernel '{k}'. Must be one of: {list(_STR)}")
+                k = _STR[k.lower()]()
+            if not isinstance(k, KernelNode):
+                raise ValueError(f"All kernels must be KernelNode objects or kernel strings, got {type(k)}")
+            ks.append(k)
+        if not ks:
+            raise ValueError("need at least one latent kernel")
+        self.kernels = ks
+        self.num_latents = len(ks)
+        self.num_probes = num_probes
+        self.max_cg_iter = max_cg_iterations
+        self.cg_tol = cg_tolerance
+        self.max_tridiag_iter = max_tridiag_iterations
+        self.ard = ard
+        self.init_mean = init_mean
+        self.device = device
+        self._lmc: Optional[LMC] = None
+
+    def _state_to_A(self, L, raw_L_diag, raw_var):
+        R, T = self.num_latents, self.T
+        A = np.zeros((R, T, T))
+        L = L.copy()
+        for s in range(R):
+            for i in range(T):
+                L[s, i, i] = _sp(raw_L_diag[s, i])
+            A[s] = L[s] @ L[s].T + np.diag([_sp(v) for v in raw_var[s]])
+        return A, L
+
+    def fit(self, X, Y, max_iterations: int = 100, learning_rate: float = 0.05,
+            initial_noise: float = 0.1, method: str = "matrix_free", verbose: bool = False):
+        if method not in ("matrix_free", "auto"):
+            raise NotImplementedError(f"method={method!r}: this build implements matrix-free LMC")
+        X = np.ascontiguousarray(X, np.float32)
+        if X.ndim == 1:
+            X = X[:, None]
+        Y = np.asarray(Y, np.float32)
+        if Y.ndim != 2 or Y.shape[0] != X.shape[0]:
+            raise ValueError("Y must be [n, T] with the rows of X")
+        n, d = X.shape
+        T = Y.shape[1]
+        R = self.num_latents
+        self.T, self.dim = T, d
+        self._X = X
+        self.kernels_resolved = [make_ard_kernel(k, d) if self.ard else k.resolve_ard(d)
+                                 for k in self.kernels]
+        params0 = [k.get_initial_params() for k in self.kernels_resolved]
+        masks = [k.engine_trainable_mask() for k in self.kernels_resolved]
+        provs = [Provider(X, k, p, 0.0, device=self.device)
+                 for k, p in zip(self.kernels_resolved, params0)]
+        self._lmc = LMC(provs, T)
+        raw_p = [np.array([_isp(float(v)) for v in p]) for p in params0]
+        raw_noise = np.array([_isp(initial_noise)] * T)
+        if self.init_mean is None:
+            raw_mean = Y.mean(axis=0).astype(np.float64)
+        else:
+            raw_mean = np.broadcast_to(np.asarray(self.init_mean, np.float64), (T,)).copy()
+        init_diag = math.sqrt(1.0 / R)
+        L = np.zeros((R, T, T))
+        for s in range(R):
+            for i in range(T):
+                for j in range(i):
+                    L[s, i, j] = 0.01 * (s + 1) / R
+        raw_L_diag = np.full((R, T), _isp(init_diag))
+        raw_var = np.full((R, T), _isp(0.1))
+        sizes = [len(p) for p in raw_p]
+        n_adam = sum(sizes) + T + R * T * T + R * T + T
+        m = np.zeros(n_adam)
+        v = np.zeros(n_adam)
+        clip = lambda g: float(np.clip(g, -10.0, 10.0)) if np.isfinite(g) else 0.0
+        Yb = Y.T.astype(np.float64)  # [T, n] task-blocked
+        best = None
+        hist = []
+        t_step = 0
+
+        def adam(idx, g):
+            m[idx] = 0.9 * m[idx] + 0.1 * g
+            v[idx] = 0.999 * v[idx] + 0.001 * g * g
+            mh = m[idx] / (1 - 0.9 ** t_step)
+            vh = v[idx] / (1 - 0.999 ** t_step)
+            return -learning_rate * mh / (math.sqrt(vh) + 1e-8)
+
+        for it in range(max_iterations):
+            t_step += 1
+            for s in range(R):
+                provs[s].update_params(np.array([_sp(r) for r in raw_p[s]], np.float32))
+            A, Lf = self._state_to_A(L, raw_L_diag, raw_var)
+            noise = np.array([_sp(r) for r in raw_noise])
+            self._lmc.set_coregion(A, noise)
+            yc = (Yb - raw_mean[:, None]).astype(np.float32)
+            res = self._lmc.bbmm(yc, self.num_probes, self.max_cg_iter, self.max_tridiag_iter,
+                                 self.cg_tol, it, it > 0)
+            nll = res["nll"]
+            hist.append(nll)
+            if not np.isfinite(nll):
+                if best is None:
+                    raise FloatingPointError("LMC NLL is not finite at the initial parameters")
+                raw_p, raw_noise, raw_mean, L, raw_L_diag, raw_var = [np.copy(x) if not isinstance(x, list) else [np.copy(y) for y in x] for x in best[1:7]]
+                raw_var = raw_var + 0.7
+                continue
+            if best is None or nll < best[0]:
+                best = (nll, [np.copy(r) for r in raw_p], raw_noise.copy(), raw_mean.copy(),
+                        L.copy(), raw_L_diag.copy(), raw_var.copy())
+            idx = 0
+            off = 0
+            for s in range(R):
+                for q in range(sizes[s]):
+                    if masks[s][q]:
+                        g = clip(res["kgrads"][off + q]) * _dsp(raw_p[s][q])
+                        raw_p[s][q] += adam(idx, g)
+                    idx += 1
+                off += sizes[s]
+            for t in range(T):
+                raw_noise[t] += adam(idx, clip(res["gnoise"][t]) * _dsp(raw_noise[t]))
+                idx += 1
+            gA = res["gA"]
+            for s in range(R):
+                for i in range(T):
+                    for j in range(i + 1):
+                        gL = clip(2.0 * float(gA[s, i, :] @ Lf[s][:, j]))
+                        if i == j:
+                            raw_L_diag[s, i] += adam(idx, gL * _dsp(raw_L_diag[s, i]))
+                        else:
+                            L[s, i, j] += adam(idx, gL)
+                        idx += 1
+                    idx += T - i - 1
+            for s in range(R):
+                for i in range(T):
+                    raw_var[s, i] += adam(idx, clip(gA[s, i, i]) * _dsp(raw_var[s, i]))
+                    idx += 1
+            for t in range(T):
+                raw_mean[t] += adam(idx, clip(-res["sum_alpha"][t] / (n * T)))
+                idx += 1
+            if verbose and (it < 5 or it % 10 == 0):
+                print(f"LMC iter {it}: NLL = {nll:.6f}")
+        _, raw_p, raw_noise, raw_mean, L, raw_L_diag, raw_var = best
+        for s in range(R):
+            provs[s].update_params(np.array([_sp(r) for r in raw_p[s]], np.float32))
+        A, _ = self._state_to_A(L, raw_L_diag, raw_var)
+        noise = np.array([_sp(r) for r in raw_noise])
+        self._lmc.set_coregion(A, noise)
+        self.A, self.noise, self.mean_ = A, noise, raw_mean
+        self.params_ = [np.array([_sp(r) for r in rp]) for rp in raw_p]
+        self.nll_history = np.array(hist)
+        self.final_nll = best[0]
+        yc = (Yb - raw_mean[:, None]).astype(np.float32)
+        self._alpha, _ = self._lmc.solve(yc, 300, 1e-3)
+        return self
+
+    def log_marginal_likelihood(self) -> float:
+        return -float(self.final_nll)
+
+    def predict(self, X_test, return_var: bool = False):
+        if self._lmc is None:
+            raise RuntimeError("model must be fit first")
+        if return_var:
+            raise NotImplementedError("LMC predictive variance is not built in this round")
+        Xt = np.ascontiguousarray(X_test, np.float32)
+        if Xt.ndim == 1:
+            Xt = Xt[:, None]
+        T, n = self.T, self._X.shape[0]
+        alpha = self._alpha.reshape(T, n).T  # [n, T]
+        mean = np.zeros((Xt.shape[0], T))
+        for s, prov in enumerate(self._lmc.providers):
+            Cs = prov.cross_matvec_host(Xt, alpha)  # [n*, T] = K_s(X*, X) alpha_j
+            mean += Cs @ self.A[s].T
+        return (mean + self.mean_[None, :]).astype(np.float32)
