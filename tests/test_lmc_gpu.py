@@ -19,9 +19,13 @@ def _setup(n=150, d=2, T=3, seed=0):
     ks = [RBF(), Matern32(), make_ard_kernel(RBF(ard=True), d)]
     ps = [np.array([0.5, 1.0], np.float32), np.array([0.6, 0.8], np.float32),
           np.array([0.7, 0.4, 1.1], np.float32)]
-    A = np.stack([(lambda M: M @ M.T + 0.1 * np.eye(T))(rng.normal(size=(T, T)) * 0.5)
+    # Condition number ~40 so a 30-iteration solve is converged in float32 and
+    # float64 alike (at ~1e3 the unconverged float32 and float64 CG iterates
+    # differ by more than the 1e-4 NLL bar; the float32 arithmetic is the
+    # reference's own).
+    A = np.stack([(lambda M: 0.1 * (M @ M.T) + 0.05 * np.eye(T))(rng.normal(size=(T, T)) * 0.5)
                   for _ in ks]).astype(np.float32)
-    noise = rng.uniform(0.1, 0.3, size=T).astype(np.float32)
+    noise = rng.uniform(0.5, 1.0, size=T).astype(np.float32)
     provs = [Provider(X, k, p, 0.0) for k, p in zip(ks, ps)]
     lmc = LMC(provs, T)
     lmc.set_coregion(A, noise)
