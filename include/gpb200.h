@@ -316,6 +316,13 @@ int gpb_lmc_bbmm(gpb_lmc* h, const float* y_centered_host, int32_t num_probes, i
 int gpb_lmc_solve(gpb_lmc* h, const float* rhs_host, int32_t max_cg_iter, float cg_tol,
                   float* x_host_out, int32_t* iters_out);
 
+/* Tensor-core self-test (no reference counterpart): one 128x16x8 tcgen05
+ * kind::tf32 MMA from shared-memory operands, A [128][8], B [16][8] row-major
+ * host arrays, D = A B^T [128][16]. variant 0 = the operand layout the
+ * library's tensor-core kernels use. */
+int gpb_tc_selftest(int32_t device, int32_t variant, const float* a_host, const float* b_host,
+                    float* d_host);
+
 /* Same result as gpb_forward_matvec, but the call allocates no device memory:
  * all scratch lives in one fixed 32 MiB array compiled into the library, held
  * on every GPU that uses it until the process exits. For callers that must

@@ -118,12 +118,12 @@ int Engine::matvec(float* v_local, int64_t v_ld, int t, float* out, int64_t out_
     const int rem = t - c0;
     const int T = kv_pick_t(rem);
     const int tcols = std::min(rem, T);
-    const bool dup = kv_uses_x2(p->eval, p->DP, T);
+    const int layout = kv_layout(p->eval, p->DP, T);
     const int W = kv_packed_width(p->eval, p->DP, T);
     GPB_TRY(xv.ensure((size_t)rows_total * W * sizeof(float)));
     float* mine = xv.f() + (int64_t)dist.rank * nl_pad * W;
     GPB_TRY(k_pack(p->Xs_d + r0 * p->DP, p->DP, v_local, v_ld, c0, tcols, T, nl, nl_pad, mine,
-                   update_z, update_beta, st, dup));
+                   update_z, update_beta, st, layout));
     p->launches += 1;
     if (world > 1) {
       ncclResult_t r = ncclAllGather(mine, xv.f(), (size_t)nl_pad * W, ncclFloat, dist.comm, st);

@@ -91,7 +91,7 @@ int k_scale_cols(float* v, int64_t ld, int64_t nl, int t, const float* scale, in
                  cudaStream_t st);
 int k_pack(const float* xs, int DP, float* v, int64_t v_ld, int c0, int tcols, int T, int64_t nl,
            int64_t nl_pad, float* dst, const float* upd_z, const float* upd_beta,
-           cudaStream_t st, bool dup = false);
+           cudaStream_t st, int layout = 0);
 int k_coldots(int npairs, const float* const* a, const float* const* b, int64_t ld, int64_t nl,
               int t, Reducer& red, cudaStream_t st);
 int k_cg_alpha(const float* rz_old, const double* pap, float* alpha, float* alpha_hist, int t,

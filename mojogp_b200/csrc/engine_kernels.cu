@@ -4,6 +4,7 @@
 // blocks [t][ld] over the rank's local rows.
 #include "engine.cuh"
 #include "train.cuh"
+#include "matvec.cuh"
 
 namespace gpb {
 
@@ -155,8 +156,11 @@ __global__ void pack_rows_kernel(const float* __restrict__ xs, int DP, float* __
 }
 int k_pack(const float* xs, int DP, float* v, int64_t v_ld, int c0, int tcols, int T, int64_t nl,
            int64_t nl_pad, float* dst, const float* upd_z, const float* upd_beta,
-           cudaStream_t st, bool dup) {
+           cudaStream_t st, int layout) {
   if (nl_pad <= 0) return GPB_OK;
+  if (layout == KV_TC)
+    return launch_pack_tc(xs, DP, v, v_ld, c0, tcols, nl, nl_pad, dst, upd_z, upd_beta, st);
+  const bool dup = layout == KV_X2;
   pack_rows_kernel<<<(unsigned)ceil_div(nl_pad, 256), 256, 0, st>>>(
       xs, DP, v, v_ld, c0, tcols, dup ? 2 * (DP + T) : packed_width(DP, T), nl, nl_pad, dst, upd_z,
       upd_beta, dup);

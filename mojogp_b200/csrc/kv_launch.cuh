@@ -56,15 +56,30 @@ inline int kv_pick_t(int64_t remaining) {
   return 1;
 }
 
-// Paired-row FFMA2 kernel (kv_tiles_x2.cuh) for fast leaves with an even DP
-// and T >= 4; GPB_KV_SCALAR=1 in the environment forces the scalar kernel.
+// Kernel / packed-layout choice per launch shape:
+//   KV_TC     tensor-core contraction (kv_tiles_tc.cuh): fast leaves, T = 16,
+//             DP a multiple of 4; GPB_KV_TC=0 in the environment disables it;
+//   KV_X2     paired-row FFMA2 kernel (kv_tiles_x2.cuh): fast leaves, even DP,
+//             T >= 4; GPB_KV_SCALAR=1 disables it (and the TC kernel);
+//   KV_SCALAR everything else (and the composite-tree evaluator).
+enum KvLayout { KV_SCALAR = 0, KV_X2 = 1, KV_TC = 2 };
 bool kv_x2_disabled();
-inline bool kv_uses_x2(int eval, int DP, int T) {
-  return eval != kEvalGeneric && DP % 2 == 0 && T >= 4 && !kv_x2_disabled();
+bool kv_tc_disabled();
+inline int kv_layout(int eval, int DP, int T) {
+  if (eval == kEvalGeneric || kv_x2_disabled()) return KV_SCALAR;
+  if (T == 16 && DP % 4 == 0 && DP <= 32 && !kv_tc_disabled()) return KV_TC;
+  if (DP % 2 == 0 && T >= 4) return KV_X2;
+  return KV_SCALAR;
 }
-// Floats per packed column row for this launch shape.
+inline bool kv_uses_x2(int eval, int DP, int T) { return kv_layout(eval, DP, T) == KV_X2; }
+// Floats per packed column row for this launch shape (the TC layout is
+// tile-blocked, 128 rows per tile, with the same average width).
 inline int kv_packed_width(int eval, int DP, int T) {
-  return kv_uses_x2(eval, DP, T) ? 2 * (DP + T) : ((DP + T) + 3) / 4 * 4;
+  switch (kv_layout(eval, DP, T)) {
+    case KV_TC: return DP + 32;
+    case KV_X2: return 2 * (DP + T);
+    default: return ((DP + T) + 3) / 4 * 4;
+  }
 }
 
 // Rows per thread for a (DP, T, generic) instantiation.

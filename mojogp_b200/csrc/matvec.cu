@@ -2,6 +2,7 @@
 // prescaling and column packing for the tiled K·V kernels.
 #include "kv_launch.cuh"
 #include "matvec.cuh"
+#include "kv_tiles_tc.cuh"
 
 #include <cstdlib>
 
@@ -125,6 +126,58 @@ __global__ void pack_dup_kernel(const float* __restrict__ xs, int DP, const floa
   }
 }
 
+bool kv_tc_disabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("GPB_KV_TC");
+    v = (e && e[0] == '0') ? 1 : 0;
+  }
+  return v == 1;
+}
+
+// Tensor-core tile layout (kv_tiles_tc.cuh): per 128-row tile
+// [x' 128 x DP][V hi: 16 k-steps x 128][V lo: 16 k-steps x 128].
+__global__ void pack_tc_kernel(const float* __restrict__ xs, int DP, float* __restrict__ v,
+                               int64_t v_ld, int c0, int tcols, int64_t n, int64_t npad,
+                               float* __restrict__ dst, const float* __restrict__ upd_z,
+                               const float* __restrict__ upd_beta) {
+  const int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (j >= npad) return;
+  const int TILE = 128 * DP + 2 * 16 * 128;
+  float* base = dst + (j / 128) * TILE;
+  const int jt = (int)(j % 128);
+  const int ks = jt / 8, k = jt % 8;
+  float* bh = base + 128 * DP + ks * 128;
+  float* bl = bh + 16 * 128;
+  for (int q = 0; q < DP; ++q) base[jt * DP + q] = (j < n) ? xs[j * DP + q] : 0.f;
+  for (int c = 0; c < 16; ++c) {
+    float val = 0.f;
+    if (j < n && c < tcols) {
+      const int64_t off = (int64_t)(c0 + c) * v_ld + j;
+      val = v[off];
+      if (upd_beta) {
+        const float b = upd_beta[c0 + c];
+        const float zz = upd_z[off];
+        val = (b == 0.f || b != b || val != val) ? zz : fmaf(b, val, zz);
+        v[off] = val;
+      }
+    }
+    const float hi = tf32_hi(val);
+    bh[tc_b_offset(c, k)] = hi;
+    bl[tc_b_offset(c, k)] = val - hi;
+  }
+}
+
+int launch_pack_tc(const float* xs, int DP, float* v, int64_t v_ld, int c0, int tcols, int64_t n,
+                   int64_t npad, float* xv, const float* upd_z, const float* upd_beta,
+                   cudaStream_t stream) {
+  if (npad == 0) return GPB_OK;
+  pack_tc_kernel<<<(unsigned)ceil_div(npad, 256), 256, 0, stream>>>(xs, DP, v, v_ld, c0, tcols, n,
+                                                                   npad, xv, upd_z, upd_beta);
+  GPB_CHECK_CUDA(cudaGetLastError());
+  return GPB_OK;
+}
+
 bool kv_x2_disabled() {
   static int v = -1;
   if (v < 0) {
@@ -135,10 +188,13 @@ bool kv_x2_disabled() {
 }
 
 int launch_pack(const float* xs, int DP, const float* v, int64_t v_ld, int tcols, int T, int64_t n,
-                int64_t npad, float* xv, cudaStream_t stream, bool dup) {
+                int64_t npad, float* xv, cudaStream_t stream, int layout) {
   const int W = packed_width(DP, T);
   if (npad == 0) return GPB_OK;
-  if (dup) {
+  if (layout == KV_TC)
+    return launch_pack_tc(xs, DP, const_cast<float*>(v), v_ld, 0, tcols, n, npad, xv, nullptr,
+                          nullptr, stream);
+  if (layout == KV_X2) {
     pack_dup_kernel<<<(unsigned)ceil_div(npad, 256), 256, 0, stream>>>(xs, DP, v, v_ld, tcols, T,
                                                                       n, npad, xv);
     GPB_CHECK_CUDA(cudaGetLastError());

@@ -14,8 +14,14 @@ struct PrescaleSpec {
 
 int launch_prescale(const float* X, int64_t n, int d, const PrescaleSpec& ps, float* xs,
                     cudaStream_t stream);
-// dup = paired-row layout ([-x, -x, ..., v, v, ...], width 2 (DP + T)).
+// layout = KvLayout: scalar rows, paired rows ([-x, -x, ..., v, v, ...]) or
+// tensor-core tiles ([x' | V hi | V lo] per 128 rows).
 int launch_pack(const float* xs, int DP, const float* v, int64_t v_ld, int tcols, int T, int64_t n,
-                int64_t npad, float* xv, cudaStream_t stream, bool dup = false);
+                int64_t npad, float* xv, cudaStream_t stream, int layout = 0);
+// Tensor-core tile packing with optional in-place p = z + beta p update
+// (columns c0 .. c0+tcols of v).
+int launch_pack_tc(const float* xs, int DP, float* v, int64_t v_ld, int c0, int tcols, int64_t n,
+                   int64_t npad, float* xv, const float* upd_z, const float* upd_beta,
+                   cudaStream_t stream);
 
 }  // namespace gpb

@@ -76,7 +76,7 @@ extern "C" int gpb_forward_matvec_noalloc(gpb_provider* p, float* out_dev, const
     const int T = kv_pick_t(rem);
     const int tcols = (int)std::min<int64_t>(rem, T);
     GPB_TRY(launch_pack(xs, DP, v_dev + c0 * n, n, tcols, T, n, npad, xv, st,
-                        kv_uses_x2(p->eval, DP, T)));
+                        kv_layout(p->eval, DP, T)));
     KvLaunch L{};
     L.eval = p->eval;
     L.DP = DP;

@@ -242,7 +242,7 @@ int provider_kv(gpb_provider* p, const float* xrow, int64_t nrow, const float* v
     void* xv = nullptr;
     GPB_TRY(p->ws.get(WS_XV, (size_t)npad * W * sizeof(float), &xv));
     GPB_TRY(launch_pack(p->Xs_d, p->DP, v + c0 * v_ld, v_ld, tcols, T, p->n, npad, (float*)xv,
-                        stream, kv_uses_x2(p->eval, p->DP, T)));
+                        stream, kv_layout(p->eval, p->DP, T)));
     p->launches += 1;
     const int64_t part_floats = std::min<int64_t>((int64_t)32 * T * nrow, (int64_t)1 << 29);
     void* part = nullptr;
