@@ -32,7 +32,7 @@ int kv_launch_tc(const KvLaunch& L) {
   if (dev < 0 || dev >= 64) dev = 0;
   if (!init[dev]) {
     GPB_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    GPB_CHECK_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&resident[dev], kern, kTcThreads, smem));
+    GPB_CHECK_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&resident[dev], kern, kTcThreads + 32, smem));
     GPB_CHECK_CUDA(cudaDeviceGetAttribute(&num_sms[dev], cudaDevAttrMultiProcessorCount, dev));
     if (resident[dev] < 1) resident[dev] = 1;
     init[dev] = true;
@@ -54,7 +54,7 @@ int kv_launch_tc(const KvLaunch& L) {
     ep.out_ld = L.nrow;
   }
   if (L.ev_begin) GPB_CHECK_CUDA(cudaEventRecord(L.ev_begin, L.stream));
-  kern<<<dim3((unsigned)row_blocks, (unsigned)splits), kTcThreads, smem, L.stream>>>(
+  kern<<<dim3((unsigned)row_blocks, (unsigned)splits), kTcThreads + 32, smem, L.stream>>>(
       L.xrow, L.nrow, L.xv, L.ntiles, tiles_per_split, L.fp, ep, L.err);
   GPB_CHECK_CUDA(cudaGetLastError());
   if (L.launches) *L.launches += 1;

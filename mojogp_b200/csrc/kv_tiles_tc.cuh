@@ -25,12 +25,12 @@
 namespace gpb {
 
 constexpr int kTcStages = 2;       // column-tile ring depth
-constexpr int kTcChunk = 16;       // columns per K block (2 MMA k-steps)
-constexpr int kTcRows = 2;         // row tiles (M = 128 each) per CTA
+constexpr int kTcChunk = 8;        // columns per K block (one MMA k-step)
+constexpr int kTcRows = 4;         // row tiles (M = 128 each) per CTA
 constexpr int kTcThreads = 128;
 constexpr int kTcAStageBytes = kTcRows * 2 * 128 * kTcChunk * 4;  // hi + lo, both row tiles
 
-// Packed tile: [x' : 128 x DP][V hi : 16 k-steps x 128][V lo : 16 k-steps x 128] floats.
+// Packed tile: [-x' : 128 x DP][V hi : 16 k-steps x 128][V lo : 16 k-steps x 128] floats.
 __host__ __device__ constexpr int tc_tile_floats(int DP) { return 128 * DP + 2 * 16 * 128; }
 
 // Offset (floats) of element (n, k) inside one 8-column k-step of the B block:
@@ -44,177 +44,210 @@ __device__ __forceinline__ float tf32_hi(float x) {
 }
 
 template <int DP, int LEAF>
-__global__ void __launch_bounds__(kTcThreads) kv_tile_tc_kernel(
+__global__ void __launch_bounds__(kTcThreads + 32, 2) kv_tile_tc_kernel(
     const float* __restrict__ xrow, int64_t nrow, const float* __restrict__ xv, int ntiles_total,
     int tiles_per_split, const __grid_constant__ FastParams fp, TileEpilogue ep, int* err) {
+  // Warps 0-3 form K blocks (one row per thread and row tile); warp 4 is the
+  // producer: it streams column tiles (TMA), issues the MMAs once a K block is
+  // complete, and refills ring slots when both the x' reads and the MMAs that
+  // read the slot's V blocks are done. Hand-offs use mbarriers only.
   constexpr int TILE = tc_tile_floats(DP);
   extern __shared__ __align__(1024) float smem[];
-  float* ring_buf = smem;                                         // kTcStages x TILE
-  float* abuf = smem + kTcStages * TILE;                           // 2 stages x kTcAStageBytes
-  __shared__ __align__(8) uint64_t ring_bars[kTcStages];
-  __shared__ __align__(8) uint64_t mma_bars[2];
+  float* ring_buf = smem;
+  float* abuf = smem + kTcStages * TILE;
+  __shared__ __align__(8) uint64_t full_bar[kTcStages];   // TMA landed
+  __shared__ __align__(8) uint64_t xdone_bar[kTcStages];  // 128 threads done with x'
+  __shared__ __align__(8) uint64_t afull_bar[2];          // 128 threads wrote a K block
+  __shared__ __align__(8) uint64_t mma_bar[2];            // tensor core consumed a K block
   __shared__ uint32_t tslot;
+  __shared__ int abort_flag;
 
   const int tid = threadIdx.x;
+  const int warp = tid >> 5, lane = tid & 31;
   const int split = blockIdx.y;
   const int t0 = split * tiles_per_split;
   const int ntiles = max(0, min(ntiles_total, t0 + tiles_per_split) - t0);
+  constexpr int kChunks = 128 / kTcChunk;
 
   if (tid == 0) {
-    mbar_init(&mma_bars[0], 1);
-    mbar_init(&mma_bars[1], 1);
+    for (int s = 0; s < kTcStages; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&xdone_bar[s], kTcThreads);
+    }
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&afull_bar[s], kTcThreads);
+      mbar_init(&mma_bar[s], 1);
+    }
+    abort_flag = 0;
+    fence_barrier_init();
   }
-  if (tid < 32) tmem_alloc(&tslot, 32);  // 2 row tiles x 16 fp32 columns
-  TileRingT<kTcStages> ring{ring_buf, ring_bars, xv, t0, ntiles, (uint32_t)TILE};
-  ring.start();  // inits ring barriers, fences, __syncthreads, issues first copies
+  if (warp == 4) tmem_alloc(&tslot, 16 * kTcRows);  // power of two >= 32
+  tc_fence_before();
+  __syncthreads();
   tc_fence_after();
   const uint32_t tmem = tslot;
+  const uint32_t tile_bytes = TILE * sizeof(float);
 
-  const int64_t row0 = (int64_t)blockIdx.x * (128 * kTcRows) + tid;
-  float xi[kTcRows][DP];
-#pragma unroll
-  for (int r = 0; r < kTcRows; ++r) {
-    const int64_t i = row0 + (int64_t)r * 128;
-#pragma unroll
-    for (int k = 0; k < DP; ++k) xi[r][k] = (i < nrow) ? xrow[i * DP + k] : 0.f;
-  }
-  const uint32_t idesc = make_idesc_tf32(128, 16);
-  // This thread's row inside a K block: core-matrix row (tid/8, tid%8).
-  const int a_row_off = (tid / 8) * 32 + (tid % 8) * 4;  // floats
-  bool failed = false;
-  int g = 0;  // global chunk counter
-  for (int kt = 0; kt < ntiles && !failed; ++kt) {
-    const float* tile = ring.acquire(kt);
-    if (tile == nullptr) {
-      failed = true;
-      break;
-    }
-    const float* xs = tile;
-    const float* bhi = tile + 128 * DP;
-    const float* blo = bhi + 16 * 128;
-    for (int q = 0; q < 128 / kTcChunk; ++q, ++g) {
-      const int st = g & 1;
-      float* ablk = abuf + st * (kTcAStageBytes / 4);
-      if (g >= 2) {
-        const bool ok = mbar_wait_bounded(&mma_bars[st], ((g - 2) >> 1) & 1);
-        if (!__syncthreads_and(ok)) {
-          failed = true;
-          break;
-        }
-        tc_fence_after();
+  if (warp == 4) {
+    if (lane == 0) {
+      for (int s = 0; s < kTcStages && s < ntiles; ++s) {
+        mbar_arrive_expect_tx(&full_bar[s], tile_bytes);
+        bulk_copy_g2s(ring_buf + s * TILE, xv + (int64_t)(t0 + s) * TILE, tile_bytes, &full_bar[s]);
       }
-#pragma unroll
-      for (int j4 = 0; j4 < kTcChunk; j4 += 4) {
-        float kv[kTcRows][4];
-#pragma unroll
-        for (int jj = 0; jj < 4; ++jj) {
-          const float4* xr = reinterpret_cast<const float4*>(xs + (q * kTcChunk + j4 + jj) * DP);
-          float xj[DP];
-#pragma unroll
-          for (int k = 0; k < DP; k += 4) {
-            const float4 v = xr[k / 4];
-            xj[k] = v.x; xj[k + 1] = v.y; xj[k + 2] = v.z; xj[k + 3] = v.w;
-          }
+      const uint32_t idesc = make_idesc_tf32(128, 16);
+      int g = 0;
+      bool ok = true;
+      for (int kt = 0; kt < ntiles && ok; ++kt) {
+        const int slot = kt % kTcStages;
+        const float* tile = ring_buf + slot * TILE;
+        const float* bhi = tile + 128 * DP;
+        const float* blo = bhi + 16 * 128;
+        ok = mbar_wait_bounded(&full_bar[slot], (kt / kTcStages) & 1);
+        for (int q = 0; q < kChunks && ok; ++q, ++g) {
+          const int st = g & 1;
+          ok = mbar_wait_bounded(&afull_bar[st], (g >> 1) & 1);
+          if (!ok) break;
+          tc_fence_after();
+          const float* ablk = abuf + st * (kTcAStageBytes / 4);
 #pragma unroll
           for (int r = 0; r < kTcRows; ++r) {
-            float u0 = 0.f, u1 = 0.f;
-#pragma unroll
-            for (int k = 0; k < DP; k += 2) {
-              const float d0 = xi[r][k] - xj[k];
-              u0 = fmaf(d0, d0, u0);
-              const float d1 = xi[r][k + 1] - xj[k + 1];
-              u1 = fmaf(d1, d1, u1);
-            }
-            kv[r][jj] = FastEval<LEAF>::value(u0 + u1, fp);
-          }
-        }
-#pragma unroll
-        for (int r = 0; r < kTcRows; ++r) {
-          float4 hi, lo;
-          hi.x = tf32_hi(kv[r][0]); lo.x = kv[r][0] - hi.x;
-          hi.y = tf32_hi(kv[r][1]); lo.y = kv[r][1] - hi.y;
-          hi.z = tf32_hi(kv[r][2]); lo.z = kv[r][2] - hi.z;
-          hi.w = tf32_hi(kv[r][3]); lo.w = kv[r][3] - hi.w;
-          // K block (row tile r): hi at r*2*2048 floats, lo right after; k-group j4/4.
-          float* base = ablk + r * 2 * (128 * kTcChunk) + (j4 / 4) * 512 + a_row_off;
-          *reinterpret_cast<float4*>(base) = hi;
-          *reinterpret_cast<float4*>(base + 128 * kTcChunk) = lo;
-        }
-      }
-      fence_proxy_async_smem();
-      tc_fence_before();
-      __syncthreads();
-      if (tid == 0) {
-        tc_fence_after();
-#pragma unroll
-        for (int r = 0; r < kTcRows; ++r) {
-          const float* ahi = ablk + r * 2 * (128 * kTcChunk);
-          const float* alo = ahi + 128 * kTcChunk;
-          const uint32_t d = tmem + r * 16;
-#pragma unroll
-          for (int ks = 0; ks < 2; ++ks) {
-            const int kstep = q * 2 + ks;  // 8-column step inside the 128-column tile
-            const uint64_t dah = make_smem_desc(ahi + ks * 1024, 2048, 128);
-            const uint64_t dal = make_smem_desc(alo + ks * 1024, 2048, 128);
-            const uint64_t dbh = make_smem_desc(bhi + kstep * 128, 256, 128);
-            const uint64_t dbl = make_smem_desc(blo + kstep * 128, 256, 128);
-            const uint32_t acc0 = (g > 0 || ks > 0) ? 1u : 0u;
-            mma_tf32(d, dah, dbh, idesc, acc0);
+            const float* ahi = ablk + r * 2 * (128 * kTcChunk);
+            const float* alo = ahi + 128 * kTcChunk;
+            const uint32_t d = tmem + r * 16;
+            static_assert(kTcChunk == 8, "one MMA k-step per K block");
+            const uint64_t dah = make_smem_desc(ahi, 2048, 128);
+            const uint64_t dal = make_smem_desc(alo, 2048, 128);
+            const uint64_t dbh = make_smem_desc(bhi + q * 128, 256, 128);
+            const uint64_t dbl = make_smem_desc(blo + q * 128, 256, 128);
+            mma_tf32(d, dah, dbh, idesc, g > 0 ? 1u : 0u);
             mma_tf32(d, dah, dbl, idesc, 1u);
             mma_tf32(d, dal, dbh, idesc, 1u);
           }
+          mma_commit(&mma_bar[st]);
         }
-        mma_commit(&mma_bars[st]);
+        if (ok && kt + kTcStages < ntiles) {
+          ok = mbar_wait_bounded(&xdone_bar[slot], (kt / kTcStages) & 1) &&
+               mbar_wait_bounded(&mma_bar[(g - 1) & 1], ((g - 1) >> 1) & 1);
+          if (ok) {
+            mbar_arrive_expect_tx(&full_bar[slot], tile_bytes);
+            bulk_copy_g2s(ring_buf + slot * TILE, xv + (int64_t)(t0 + kt + kTcStages) * TILE,
+                          tile_bytes, &full_bar[slot]);
+          }
+        }
+      }
+      if (!ok) {
+        atomicExch(err, DEV_WAIT_TIMEOUT);
+        atomicExch(&abort_flag, 1);
       }
     }
-    if (failed) break;
-    // The ring slot may be refilled once the tensor core has read its V
-    // blocks: wait for the commit of this tile's last chunk (thread 0 only,
-    // before it issues the next copy inside release()).
-    if (tid == 0 && kt + kTcStages < ntiles) {
-      const int gl = g - 1;
-      if (!mbar_wait_bounded(&mma_bars[gl & 1], (gl >> 1) & 1)) atomicExch(err, DEV_WAIT_TIMEOUT);
+  } else {
+    const int64_t row0 = (int64_t)blockIdx.x * (128 * kTcRows) + tid;
+    // Row pairs (2p, 2p+1) share float2 registers: the distance runs on the
+    // packed FADD2 / FFMA2 instructions against duplicated -x'_j.
+    static_assert(kTcRows % 2 == 0, "row pairs");
+    float2 xi[kTcRows / 2][DP];
+#pragma unroll
+    for (int rp = 0; rp < kTcRows / 2; ++rp) {
+      const int64_t i0 = row0 + (int64_t)(2 * rp) * 128, i1 = i0 + 128;
+#pragma unroll
+      for (int k = 0; k < DP; ++k)
+        xi[rp][k] = make_float2(i0 < nrow ? xrow[i0 * DP + k] : 0.f, i1 < nrow ? xrow[i1 * DP + k] : 0.f);
     }
-    ring.release(kt);
-  }
-
-  // Epilogue: wait for the last commit, read the accumulators from TMEM.
-  bool have = !failed && g > 0;
-  if (have) {
-    const int gl = g - 1;
-    const bool ok = mbar_wait_bounded(&mma_bars[gl & 1], (gl >> 1) & 1);
-    have = __syncthreads_and(ok);
-  } else {
-    __syncthreads();
-  }
-  tc_fence_after();
-  if (failed || (g > 0 && !have)) {
-    if (tid == 0) atomicExch(err, DEV_WAIT_TIMEOUT);
-  } else {
-    const bool partial = gridDim.y > 1;
+    const int a_row_off = (tid / 8) * 32 + (tid % 8) * 4;
+    int g = 0;
+    bool ok = true;
+    for (int kt = 0; kt < ntiles && ok; ++kt) {
+      const int slot = kt % kTcStages;
+      ok = mbar_wait_bounded(&full_bar[slot], (kt / kTcStages) & 1);
+      if (!ok) break;
+      const float* xs = ring_buf + slot * TILE;
+      for (int q = 0; q < kChunks; ++q, ++g) {
+        const int st = g & 1;
+        if (g >= 2) {
+          ok = mbar_wait_bounded(&mma_bar[st], ((g - 2) >> 1) & 1);
+          if (!ok) break;
+          tc_fence_after();
+        }
+        float* ablk = abuf + st * (kTcAStageBytes / 4);
 #pragma unroll
-    for (int r = 0; r < kTcRows; ++r) {
-      float acc[16];
-      if (g > 0) {
-        tmem_ld16(tmem + r * 16 + ((uint32_t)((tid / 32) * 32) << 16), acc);
-      } else {
+        for (int j4 = 0; j4 < kTcChunk; j4 += 4) {
+          float kv[kTcRows][4];
 #pragma unroll
-        for (int c = 0; c < 16; ++c) acc[c] = 0.f;
-      }
-      const int64_t i = row0 + (int64_t)r * 128;
-      if (i < nrow) {
+          for (int jj = 0; jj < 4; ++jj) {
+            const float4* xr = reinterpret_cast<const float4*>(xs + (q * kTcChunk + j4 + jj) * DP);
+            float2 xn[DP];
 #pragma unroll
-        for (int c = 0; c < 16; ++c) {
-          if (c >= ep.tcols) continue;
-          if (partial) {
-            ep.out[((int64_t)split * 16 + c) * ep.out_ld + i] = acc[c];
-          } else {
-            float o = ep.scale * acc[c];
-            if (ep.noise_v) {
-              const float nz = ep.noise_vec ? ep.noise_vec[i] : ep.noise;
-              o = fmaf(nz, ep.noise_v[c * ep.noise_ld + i], o);
+            for (int k = 0; k < DP; k += 4) {
+              const float4 v = xr[k / 4];
+              xn[k] = make_float2(v.x, v.x);
+              xn[k + 1] = make_float2(v.y, v.y);
+              xn[k + 2] = make_float2(v.z, v.z);
+              xn[k + 3] = make_float2(v.w, v.w);
             }
-            ep.out[c * ep.out_ld + i] = o;
+#pragma unroll
+            for (int rp = 0; rp < kTcRows / 2; ++rp) {
+              float2 u0 = make_float2(0.f, 0.f), u1 = make_float2(0.f, 0.f);
+#pragma unroll
+              for (int k = 0; k < DP; k += 2) {
+                const float2 d0 = __fadd2_rn(xi[rp][k], xn[k]);
+                u0 = __ffma2_rn(d0, d0, u0);
+                const float2 d1 = __fadd2_rn(xi[rp][k + 1], xn[k + 1]);
+                u1 = __ffma2_rn(d1, d1, u1);
+              }
+              const float2 u = __fadd2_rn(u0, u1);
+              kv[2 * rp][jj] = FastEval<LEAF>::value(u.x, fp);
+              kv[2 * rp + 1][jj] = FastEval<LEAF>::value(u.y, fp);
+            }
+          }
+#pragma unroll
+          for (int r = 0; r < kTcRows; ++r) {
+            float4 hi, lo;
+            hi.x = tf32_hi(kv[r][0]); lo.x = kv[r][0] - hi.x;
+            hi.y = tf32_hi(kv[r][1]); lo.y = kv[r][1] - hi.y;
+            hi.z = tf32_hi(kv[r][2]); lo.z = kv[r][2] - hi.z;
+            hi.w = tf32_hi(kv[r][3]); lo.w = kv[r][3] - hi.w;
+            float* base = ablk + r * 2 * (128 * kTcChunk) + (j4 / 4) * 512 + a_row_off;
+            *reinterpret_cast<float4*>(base) = hi;
+            *reinterpret_cast<float4*>(base + 128 * kTcChunk) = lo;
+          }
+        }
+        fence_proxy_async_smem();
+        mbar_arrive(&afull_bar[st]);
+      }
+      if (!ok) break;
+      mbar_arrive(&xdone_bar[slot]);
+    }
+    // Epilogue: the last commit covers every MMA of this CTA.
+    if (ok && g > 0) ok = mbar_wait_bounded(&mma_bar[(g - 1) & 1], ((g - 1) >> 1) & 1);
+    tc_fence_after();
+    if (!ok) {
+      atomicExch(err, DEV_WAIT_TIMEOUT);
+    } else {
+      const bool partial = gridDim.y > 1;
+#pragma unroll
+      for (int r = 0; r < kTcRows; ++r) {
+        float acc[16];
+        if (g > 0) {
+          tmem_ld16(tmem + r * 16 + ((uint32_t)(warp * 32) << 16), acc);
+        } else {
+#pragma unroll
+          for (int c = 0; c < 16; ++c) acc[c] = 0.f;
+        }
+        const int64_t i = row0 + (int64_t)r * 128;
+        if (i < nrow) {
+#pragma unroll
+          for (int c = 0; c < 16; ++c) {
+            if (c >= ep.tcols) continue;
+            if (partial) {
+              ep.out[((int64_t)split * 16 + c) * ep.out_ld + i] = acc[c];
+            } else {
+              float o = ep.scale * acc[c];
+              if (ep.noise_v) {
+                const float nz = ep.noise_vec ? ep.noise_vec[i] : ep.noise;
+                o = fmaf(nz, ep.noise_v[c * ep.noise_ld + i], o);
+              }
+              ep.out[c * ep.out_ld + i] = o;
+            }
           }
         }
       }
@@ -222,7 +255,7 @@ __global__ void __launch_bounds__(kTcThreads) kv_tile_tc_kernel(
   }
   tc_fence_before();
   __syncthreads();
-  if (tid < 32) tmem_dealloc(tmem, 32);
+  if (warp == 4) tmem_dealloc(tmem, 16 * kTcRows);
 }
 
 }  // namespace gpb

@@ -136,7 +136,7 @@ bool kv_tc_disabled() {
 }
 
 // Tensor-core tile layout (kv_tiles_tc.cuh): per 128-row tile
-// [x' 128 x DP][V hi: 16 k-steps x 128][V lo: 16 k-steps x 128].
+// [-x' 128 x DP][V hi: 16 k-steps x 128][V lo: 16 k-steps x 128].
 __global__ void pack_tc_kernel(const float* __restrict__ xs, int DP, float* __restrict__ v,
                                int64_t v_ld, int c0, int tcols, int64_t n, int64_t npad,
                                float* __restrict__ dst, const float* __restrict__ upd_z,
@@ -149,7 +149,7 @@ __global__ void pack_tc_kernel(const float* __restrict__ xs, int DP, float* __re
   const int ks = jt / 8, k = jt % 8;
   float* bh = base + 128 * DP + ks * 128;
   float* bl = bh + 16 * 128;
-  for (int q = 0; q < DP; ++q) base[jt * DP + q] = (j < n) ? xs[j * DP + q] : 0.f;
+  for (int q = 0; q < DP; ++q) base[jt * DP + q] = (j < n) ? -xs[j * DP + q] : 0.f;  // negated x'
   for (int c = 0; c < 16; ++c) {
     float val = 0.f;
     if (j < n && c < tcols) {
