@@ -58,7 +58,8 @@ inline int kv_pick_t(int64_t remaining) {
 
 // Kernel / packed-layout choice per launch shape:
 //   KV_TC     tensor-core contraction (kv_tiles_tc.cuh): fast leaves, T = 16,
-//             DP a multiple of 4; opt-in with GPB_KV_TC=1 in the environment;
+//             DP a multiple of 4 (default; GPB_KV_TC=0 in the environment
+//             selects KV_X2 instead);
 //   KV_X2     paired-row FFMA2 kernel (kv_tiles_x2.cuh): fast leaves, even DP,
 //             T >= 4; GPB_KV_SCALAR=1 disables it (and the TC kernel);
 //   KV_SCALAR everything else (and the composite-tree evaluator).

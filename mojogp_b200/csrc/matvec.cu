@@ -130,7 +130,7 @@ bool kv_tc_disabled() {
   static int v = -1;
   if (v < 0) {
     const char* e = getenv("GPB_KV_TC");
-    v = (e && e[0] == '1') ? 0 : 1;  // opt-in until it beats the FFMA2 kernel
+    v = (e && e[0] == '0') ? 1 : 0;  // default on; GPB_KV_TC=0 selects the FFMA2 kernel
   }
   return v == 1;
 }
