@@ -6,7 +6,9 @@
 namespace gpb {
 
 // A [128][8] and B [16][8] (row = M or N index, 8 = K) in global memory;
-// D [128][16] out. `variant` 1 swaps the LBO / SBO roles (diagnostic).
+// D [128][16] out. `variant` 1 swaps the LBO / SBO roles (diagnostic);
+// `variant` 2 stages A in TMEM (tcgen05.st, one column per k) instead of
+// shared memory.
 __global__ void __launch_bounds__(128) tc_selftest_kernel(const float* __restrict__ A,
                                                           const float* __restrict__ B,
                                                           float* __restrict__ D, int variant,
@@ -30,13 +32,26 @@ __global__ void __launch_bounds__(128) tc_selftest_kernel(const float* __restric
     mbar_init(&bar, 1);
     fence_barrier_init();
   }
-  if (tid < 32) tmem_alloc(&tslot, 32);
+  if (tid < 32) tmem_alloc(&tslot, 64);
   fence_proxy_async_smem();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t taddr = tslot;
-  if (tid == 0) {
+  if (variant == 2) {
+    uint32_t r[8];
+    for (int k = 0; k < 8; ++k) r[k] = __float_as_uint(to_tf32(A[tid * 8 + k]));
+    tmem_st8(taddr + 32 + ((uint32_t)((tid / 32) * 32) << 16), r);
+    tmem_wait_st();
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (tid == 0) {
+      const uint64_t bd = make_smem_desc(sB, 256, 128);
+      mma_tf32_tmem_a(taddr, taddr + 32, bd, make_idesc_tf32(128, 16), 0);
+      mma_commit(&bar);
+    }
+  } else if (tid == 0) {
     const uint32_t lboA = variant ? 128 : 2048, sboA = variant ? 2048 : 128;
     const uint32_t lboB = variant ? 128 : 256, sboB = variant ? 256 : 128;
     const uint64_t ad = make_smem_desc(sA, lboA, sboA);
@@ -55,7 +70,7 @@ __global__ void __launch_bounds__(128) tc_selftest_kernel(const float* __restric
   }
   tc_fence_before();
   __syncthreads();
-  if (tid < 32) tmem_dealloc(taddr, 32);
+  if (tid < 32) tmem_dealloc(taddr, 64);
 }
 
 }  // namespace gpb
