@@ -319,9 +319,15 @@ int gpb_lmc_solve(gpb_lmc* h, const float* rhs_host, int32_t max_cg_iter, float 
 /* Tensor-core self-test (no reference counterpart): one 128x16x8 tcgen05
  * kind::tf32 MMA from shared-memory operands, A [128][8], B [16][8] row-major
  * host arrays, D = A B^T [128][16]. variant 0 = the operand layout the
- * library's tensor-core kernels use. */
+ * library's tensor-core kernels use; variant 2 reads A from TMEM. */
 int gpb_tc_selftest(int32_t device, int32_t variant, const float* a_host, const float* b_host,
                     float* d_host);
+
+/* Tile kernel the forward matvec uses for its first 16 columns (no reference
+ * counterpart; diagnostics and tests): 0 scalar FFMA, 1 paired-row FFMA2,
+ * 2 tensor-core contraction, 3 Gram form (both contractions on the tensor
+ * core, chosen only for bounded prescaled input norms). */
+int gpb_matvec_layout(gpb_provider* p, int64_t ncols, int32_t* layout);
 
 /* Same result as gpb_forward_matvec, but the call allocates no device memory:
  * all scratch lives in one fixed 32 MiB array compiled into the library, held

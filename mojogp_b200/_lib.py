@@ -43,6 +43,7 @@ SIGNATURES = {
     "gpb_get_diagonal_value": [P, PF],
     "gpb_get_x_ptr": [P, PP],
     "gpb_forward_matvec": [P, P, P, c_i64],
+    "gpb_matvec_layout": [P, c_i64, P],
     "gpb_forward_matvec_rows": [P, P, P, c_i64, c_i64, c_i64],
     "gpb_forward_matvec_host": [P, P, P, c_i64],
     "gpb_cross_matvec": [P, P, P, P, c_i64, c_i64],

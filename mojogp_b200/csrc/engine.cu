@@ -118,8 +118,8 @@ int Engine::matvec(float* v_local, int64_t v_ld, int t, float* out, int64_t out_
     const int rem = t - c0;
     const int T = kv_pick_t(rem);
     const int tcols = std::min(rem, T);
-    const int layout = kv_layout(p->eval, p->DP, T);
-    const int W = kv_packed_width(p->eval, p->DP, T);
+    const int layout = kv_layout(p->eval, p->DP, T, p->gram_ok);
+    const int W = kv_packed_width(p->eval, p->DP, T, p->gram_ok);
     GPB_TRY(xv.ensure((size_t)rows_total * W * sizeof(float)));
     float* mine = xv.f() + (int64_t)dist.rank * nl_pad * W;
     GPB_TRY(k_pack(p->Xs_d + r0 * p->DP, p->DP, v_local, v_ld, c0, tcols, T, nl, nl_pad, mine,
@@ -156,6 +156,7 @@ int Engine::matvec(float* v_local, int64_t v_ld, int t, float* out, int64_t out_
     L.err = p->err_d;
     L.stream = st;
     L.launches = &p->launches;
+    L.gram_ok = p->gram_ok;
     GPB_TRY(launch_kv(L));
   }
   return GPB_OK;

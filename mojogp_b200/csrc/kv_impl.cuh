@@ -5,6 +5,7 @@
 #include "kv_launch.cuh"
 #include "kv_tiles_x2.cuh"
 #include "kv_tiles_tc.cuh"
+#include "kv_tiles_gram.cuh"
 
 namespace gpb {
 
@@ -66,13 +67,68 @@ int kv_launch_tc(const KvLaunch& L) {
   return GPB_OK;
 }
 
+template <int DP, int LEAF>
+int kv_launch_gram(const KvLaunch& L) {
+  auto kern = kv_tile_gram_kernel<DP, LEAF>;
+  const size_t smem = ((size_t)kGStages * gram_tile_floats(DP) + (size_t)kGRowTiles * 2 * 128 * DP) *
+                      sizeof(float);
+  int dev = 0;
+  GPB_CHECK_CUDA(cudaGetDevice(&dev));
+  static int resident[64];
+  static bool init[64] = {false};
+  static int num_sms[64];
+  if (dev < 0 || dev >= 64) dev = 0;
+  if (!init[dev]) {
+    GPB_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    GPB_CHECK_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&resident[dev], kern, kGThreads, smem));
+    GPB_CHECK_CUDA(cudaDeviceGetAttribute(&num_sms[dev], cudaDevAttrMultiProcessorCount, dev));
+    if (resident[dev] < 1) resident[dev] = 1;
+    // The kernel allocates all 512 TMEM columns: two CTAs must never share an SM.
+    GPB_REQUIRE(resident[dev] == 1, GPB_ERR_UNSUPPORTED, "Gram tile kernel: %d CTAs per SM",
+                resident[dev]);
+    init[dev] = true;
+  }
+  const int64_t row_blocks = ceil_div(L.nrow, kGEpiThreads);
+  if (row_blocks == 0 || L.ntiles == 0) return GPB_OK;
+  int splits = kv_choose_splits(row_blocks, L.ntiles, resident[dev], num_sms[dev]);
+  if (splits > 1) {
+    const int64_t need_per_split = (int64_t)16 * L.nrow;
+    const int64_t cap = L.partial ? L.partial_capacity / need_per_split : 0;
+    if (cap < splits) splits = (int)(cap >= 2 ? cap : 1);
+  }
+  int tiles_per_split = (int)ceil_div(L.ntiles, splits);
+  splits = (int)ceil_div(L.ntiles, tiles_per_split);
+  TileEpilogue ep = L.ep;
+  ep.tcols = L.tcols;
+  if (splits > 1) {
+    ep.out = L.partial;
+    ep.out_ld = L.nrow;
+  }
+  if (L.ev_begin) GPB_CHECK_CUDA(cudaEventRecord(L.ev_begin, L.stream));
+  kern<<<dim3((unsigned)row_blocks, (unsigned)splits), kGThreads, smem, L.stream>>>(
+      L.xrow, L.nrow, L.xv, L.ntiles, tiles_per_split, L.fp, ep, L.err);
+  GPB_CHECK_CUDA(cudaGetLastError());
+  if (L.launches) *L.launches += 1;
+  if (splits > 1) {
+    GPB_TRY(launch_kv_reduce(L, splits));
+    if (L.launches) *L.launches += 1;
+  }
+  if (L.ev_end) GPB_CHECK_CUDA(cudaEventRecord(L.ev_end, L.stream));
+  return GPB_OK;
+}
+
 template <int DP, int T, class Ev>
 int kv_launch_one(const KvLaunch& L) {
+  if constexpr (!Ev::kGeneric && T == 16 && (DP == 8 || DP == 16)) {
+    if constexpr (gram_leaf(Ev::kLeaf)) {
+      if (kv_layout(L.eval, DP, T, L.gram_ok) == KV_GRAM) return kv_launch_gram<DP, Ev::kLeaf>(L);
+    }
+  }
   if constexpr (!Ev::kGeneric && T == 16 && DP % 4 == 0 && DP <= 32) {
-    if (kv_layout(L.eval, DP, T) == KV_TC) return kv_launch_tc<DP, Ev::kLeaf>(L);
+    if (kv_layout(L.eval, DP, T, L.gram_ok) == KV_TC) return kv_launch_tc<DP, Ev::kLeaf>(L);
   }
   if constexpr (!Ev::kGeneric && DP % 2 == 0 && T >= 4) {
-    if (kv_uses_x2(L.eval, DP, T)) return kv_launch_impl<DP, T, Ev, true>(L);
+    if (kv_layout(L.eval, DP, T, L.gram_ok) == KV_X2) return kv_launch_impl<DP, T, Ev, true>(L);
   }
   return kv_launch_impl<DP, T, Ev, false>(L);
 }

@@ -29,6 +29,8 @@ struct KvLaunch {
   int64_t* launches = nullptr;      // incremented per kernel launched
   cudaEvent_t ev_begin = nullptr;   // if set: recorded around the tile kernel(s)
   cudaEvent_t ev_end = nullptr;
+  bool gram_ok = false;             // rows and columns are the provider's training
+                                    // inputs and their prescaled norms are bounded
 };
 
 // Compiled sizes.
@@ -57,17 +59,32 @@ inline int kv_pick_t(int64_t remaining) {
 }
 
 // Kernel / packed-layout choice per launch shape:
+//   KV_GRAM   both contractions on the tensor core (kv_tiles_gram.cuh): RBF,
+//             Matérn-3/2, Matérn-5/2 or RQ, T = 16, DP 8 or 16, and only when
+//             the caller vouches for bounded input norms (gram_ok);
+//             GPB_KV_GRAM=0 in the environment selects KV_TC instead;
 //   KV_TC     tensor-core contraction (kv_tiles_tc.cuh): fast leaves, T = 16,
 //             DP a multiple of 4 (default; GPB_KV_TC=0 in the environment
 //             selects KV_X2 instead);
 //   KV_X2     paired-row FFMA2 kernel (kv_tiles_x2.cuh): fast leaves, even DP,
 //             T >= 4; GPB_KV_SCALAR=1 disables it (and the TC kernel);
 //   KV_SCALAR everything else (and the composite-tree evaluator).
-enum KvLayout { KV_SCALAR = 0, KV_X2 = 1, KV_TC = 2 };
+enum KvLayout { KV_SCALAR = 0, KV_X2 = 1, KV_TC = 2, KV_GRAM = 3 };
 bool kv_x2_disabled();
 bool kv_tc_disabled();
-inline int kv_layout(int eval, int DP, int T) {
+bool kv_gram_disabled();
+// Largest max_i |x'_i|^2 (prescaled inputs) for which the Gram expansion keeps
+// the matvec within the 1e-5 relative bar (3xTF32 cross term, fp32 norms).
+constexpr float kGramMaxSqNorm = 100.f;
+constexpr bool gram_leaf(int eval) {
+  return eval == GPB_KERNEL_RBF || eval == GPB_KERNEL_MATERN32 || eval == GPB_KERNEL_MATERN52 ||
+         eval == GPB_KERNEL_RQ;
+}
+inline int kv_layout(int eval, int DP, int T, bool gram_ok = false) {
   if (eval == kEvalGeneric || kv_x2_disabled()) return KV_SCALAR;
+  if (gram_ok && gram_leaf(eval) && T == 16 && (DP == 8 || DP == 16) && !kv_tc_disabled() &&
+      !kv_gram_disabled())
+    return KV_GRAM;
   if (T == 16 && DP % 4 == 0 && DP <= 32 && !kv_tc_disabled()) return KV_TC;
   if (DP % 2 == 0 && T >= 4) return KV_X2;
   return KV_SCALAR;
@@ -75,8 +92,9 @@ inline int kv_layout(int eval, int DP, int T) {
 inline bool kv_uses_x2(int eval, int DP, int T) { return kv_layout(eval, DP, T) == KV_X2; }
 // Floats per packed column row for this launch shape (the TC layout is
 // tile-blocked, 128 rows per tile, with the same average width).
-inline int kv_packed_width(int eval, int DP, int T) {
-  switch (kv_layout(eval, DP, T)) {
+inline int kv_packed_width(int eval, int DP, int T, bool gram_ok = false) {
+  switch (kv_layout(eval, DP, T, gram_ok)) {
+    case KV_GRAM: return 2 * DP + 1 + 32;
     case KV_TC: return DP + 32;
     case KV_X2: return 2 * (DP + T);
     default: return ((DP + T) + 3) / 4 * 4;

@@ -3,6 +3,7 @@
 #include "kv_launch.cuh"
 #include "matvec.cuh"
 #include "kv_tiles_tc.cuh"
+#include "kv_tiles_gram.cuh"
 
 #include <cstdlib>
 
@@ -178,6 +179,66 @@ int launch_pack_tc(const float* xs, int DP, float* v, int64_t v_ld, int c0, int 
   return GPB_OK;
 }
 
+// Gram tile packing: per 128 columns [-2y hi | -2y lo | |y|^2 | V hi | V lo]
+// (kv_tiles_gram.cuh), with the same optional p = z + beta p update.
+__global__ void pack_gram_kernel(const float* __restrict__ xs, int DP, float* __restrict__ v,
+                                 int64_t v_ld, int c0, int tcols, int64_t n, int64_t npad,
+                                 float* __restrict__ dst, const float* __restrict__ upd_z,
+                                 const float* __restrict__ upd_beta) {
+  const int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (j >= npad) return;
+  float* base = dst + (j / 128) * gram_tile_floats(DP);
+  const int jt = (int)(j % 128);
+  float y[32];
+  for (int q = 0; q < DP; ++q) y[q] = (j < n) ? xs[j * DP + q] : 0.f;
+  for (int q = 0; q < DP; ++q) {
+    const float b = -2.f * y[q];
+    const float hi = tf32_hi(b);
+    base[gram_xoff(jt, q)] = hi;
+    base[128 * DP + gram_xoff(jt, q)] = b - hi;
+  }
+  base[256 * DP + jt] = gram_sqnorm(y, DP);
+  float* bh = base + 256 * DP + 128 + (jt / 8) * 128;
+  float* bl = bh + 16 * 128;
+  const int k = jt % 8;
+  for (int c = 0; c < 16; ++c) {
+    float val = 0.f;
+    if (j < n && c < tcols) {
+      const int64_t off = (int64_t)(c0 + c) * v_ld + j;
+      val = v[off];
+      if (upd_beta) {
+        const float b = upd_beta[c0 + c];
+        const float zz = upd_z[off];
+        val = (b == 0.f || b != b || val != val) ? zz : fmaf(b, val, zz);
+        v[off] = val;
+      }
+    }
+    const float hi = tf32_hi(val);
+    bh[tc_b_offset(c, k)] = hi;
+    bl[tc_b_offset(c, k)] = val - hi;
+  }
+}
+
+int launch_pack_gram(const float* xs, int DP, float* v, int64_t v_ld, int c0, int tcols, int64_t n,
+                     int64_t npad, float* xv, const float* upd_z, const float* upd_beta,
+                     cudaStream_t stream) {
+  if (npad == 0) return GPB_OK;
+  GPB_REQUIRE(DP % 8 == 0 && DP <= 32, GPB_ERR_INVALID, "Gram packing needs DP in {8,16,24,32}");
+  pack_gram_kernel<<<(unsigned)ceil_div(npad, 128), 128, 0, stream>>>(xs, DP, v, v_ld, c0, tcols, n,
+                                                                     npad, xv, upd_z, upd_beta);
+  GPB_CHECK_CUDA(cudaGetLastError());
+  return GPB_OK;
+}
+
+bool kv_gram_disabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("GPB_KV_GRAM");
+    v = (e && e[0] == '0') ? 1 : 0;
+  }
+  return v == 1;
+}
+
 bool kv_x2_disabled() {
   static int v = -1;
   if (v < 0) {
@@ -194,6 +255,9 @@ int launch_pack(const float* xs, int DP, const float* v, int64_t v_ld, int tcols
   if (layout == KV_TC)
     return launch_pack_tc(xs, DP, const_cast<float*>(v), v_ld, 0, tcols, n, npad, xv, nullptr,
                           nullptr, stream);
+  if (layout == KV_GRAM)
+    return launch_pack_gram(xs, DP, const_cast<float*>(v), v_ld, 0, tcols, n, npad, xv, nullptr,
+                            nullptr, stream);
   if (layout == KV_X2) {
     pack_dup_kernel<<<(unsigned)ceil_div(npad, 256), 256, 0, stream>>>(xs, DP, v, v_ld, tcols, T,
                                                                       n, npad, xv);

@@ -23,5 +23,9 @@ int launch_pack(const float* xs, int DP, const float* v, int64_t v_ld, int tcols
 int launch_pack_tc(const float* xs, int DP, float* v, int64_t v_ld, int c0, int tcols, int64_t n,
                    int64_t npad, float* xv, const float* upd_z, const float* upd_beta,
                    cudaStream_t stream);
+// Gram tile packing (KV_GRAM), same arguments.
+int launch_pack_gram(const float* xs, int DP, float* v, int64_t v_ld, int c0, int tcols, int64_t n,
+                     int64_t npad, float* xv, const float* upd_z, const float* upd_beta,
+                     cudaStream_t stream);
 
 }  // namespace gpb

@@ -5,6 +5,7 @@
 #include <new>
 
 #include "provider.cuh"
+#include "kv_tiles_gram.cuh"
 
 namespace gpb {
 
@@ -196,12 +197,38 @@ int provider_plan(gpb_provider* p) {
   return GPB_OK;
 }
 
+__global__ void max_sqnorm_kernel(const float* __restrict__ xs, int64_t n, int DP,
+                                  unsigned* __restrict__ out) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  float s = 0.f;
+  if (i < n) s = gram_sqnorm(xs + i * DP, DP);
+  for (int o = 16; o > 0; o >>= 1) s = fmaxf(s, __shfl_xor_sync(0xffffffffu, s, o));
+  // Non-negative floats order like their bit patterns; NaN maps above every finite value.
+  if ((threadIdx.x & 31) == 0) atomicMax(out, s != s ? 0xFFFFFFFFu : __float_as_uint(s));
+}
+
 int provider_refresh_xs(gpb_provider* p) {
   if (!p->xs_dirty) return GPB_OK;
   if (p->Xs_d) cudaFree(p->Xs_d);
   p->Xs_d = nullptr;
   GPB_CHECK_CUDA(cudaMalloc(&p->Xs_d, (size_t)std::max<int64_t>(p->n, 1) * p->DP * sizeof(float)));
   GPB_TRY(launch_prescale(p->X_d, p->n, p->d, p->ps, p->Xs_d, p->stream));
+  p->gram_ok = false;
+  if (p->eval != kEvalGeneric && gram_leaf(p->eval) && (p->DP == 8 || p->DP == 16) && p->n > 0) {
+    if (!p->sqnorm_d) GPB_CHECK_CUDA(cudaMalloc(&p->sqnorm_d, sizeof(unsigned)));
+    GPB_CHECK_CUDA(cudaMemsetAsync(p->sqnorm_d, 0, sizeof(unsigned), p->stream));
+    max_sqnorm_kernel<<<(unsigned)ceil_div(p->n, 256), 256, 0, p->stream>>>(p->Xs_d, p->n, p->DP,
+                                                                            p->sqnorm_d);
+    GPB_CHECK_CUDA(cudaGetLastError());
+    unsigned h = 0;
+    GPB_CHECK_CUDA(cudaMemcpyAsync(&h, p->sqnorm_d, sizeof(unsigned), cudaMemcpyDeviceToHost,
+                                   p->stream));
+    GPB_CHECK_CUDA(cudaStreamSynchronize(p->stream));
+    float hf = 0.f;
+    std::memcpy(&hf, &h, sizeof(hf));
+    p->gram_ok = h != 0xFFFFFFFFu && hf <= kGramMaxSqNorm;
+    p->launches += 1;
+  }
   p->xs_dirty = false;
   return GPB_OK;
 }
@@ -232,17 +259,19 @@ int provider_kv(gpb_provider* p, const float* xrow, int64_t nrow, const float* v
                 cudaStream_t stream) {
   if (nrow == 0 || ncols == 0) return GPB_OK;
   GPB_TRY(provider_refresh_xs(p));
+  // The Gram path's norm bound was checked for the training rows only.
+  const bool gram = p->gram_ok && xrow >= p->Xs_d && xrow < p->Xs_d + std::max<int64_t>(p->n, 1) * p->DP;
   const int64_t npad = round_up(std::max<int64_t>(p->n, 1), kJT);
   const int ntiles = (int)(npad / kJT);
   for (int64_t c0 = 0; c0 < ncols; c0 += 16) {
     const int64_t rem = ncols - c0;
     const int T = kv_pick_t(rem);
     const int tcols = (int)std::min<int64_t>(rem, T);
-    const int W = kv_packed_width(p->eval, p->DP, T);
+    const int W = kv_packed_width(p->eval, p->DP, T, gram);
     void* xv = nullptr;
     GPB_TRY(p->ws.get(WS_XV, (size_t)npad * W * sizeof(float), &xv));
     GPB_TRY(launch_pack(p->Xs_d, p->DP, v + c0 * v_ld, v_ld, tcols, T, p->n, npad, (float*)xv,
-                        stream, kv_layout(p->eval, p->DP, T)));
+                        stream, kv_layout(p->eval, p->DP, T, gram)));
     p->launches += 1;
     const int64_t part_floats = std::min<int64_t>((int64_t)32 * T * nrow, (int64_t)1 << 29);
     void* part = nullptr;
@@ -272,6 +301,7 @@ int provider_kv(gpb_provider* p, const float* xrow, int64_t nrow, const float* v
     L.err = p->err_d;
     L.stream = stream;
     L.launches = &p->launches;
+    L.gram_ok = gram;
     if (c0 == 0) L.ev_begin = p->tile_ev[0];
     if (c0 + 16 >= ncols) L.ev_end = p->tile_ev[1];
     GPB_TRY(launch_kv(L));
@@ -438,6 +468,7 @@ int gpb_provider_destroy(gpb_provider* p) {
   if (p->Xs_d) cudaFree(p->Xs_d);
   if (p->noise_vec_d) cudaFree(p->noise_vec_d);
   if (p->err_d) cudaFree(p->err_d);
+  if (p->sqnorm_d) cudaFree(p->sqnorm_d);
   if (p->stream) cudaStreamDestroy(p->stream);
   delete p;
   return GPB_OK;
@@ -522,6 +553,14 @@ int gpb_forward_matvec_rows(gpb_provider* p, float* out_dev, const float* v_dev,
   GPB_TRY(provider_refresh_xs(p));
   return provider_kv(p, p->Xs_d + row_begin * p->DP, row_end - row_begin, v_dev, p->n, ncols,
                      out_dev, row_end - row_begin, true, row_begin, p->stream);
+}
+
+int gpb_matvec_layout(gpb_provider* p, int64_t ncols, int32_t* layout) {
+  GPB_REQUIRE(p && layout && ncols > 0, GPB_ERR_INVALID, "bad arguments");
+  GPB_CHECK_CUDA(cudaSetDevice(p->device));
+  GPB_TRY(provider_refresh_xs(p));
+  *layout = kv_layout(p->eval, p->DP, kv_pick_t(ncols), p->gram_ok);
+  return GPB_OK;
 }
 
 int gpb_forward_matvec(gpb_provider* p, float* out_dev, const float* v_dev, int64_t ncols) {

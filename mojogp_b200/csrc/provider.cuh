@@ -50,6 +50,8 @@ struct gpb_provider {
   gpb::PrescaleSpec ps{};
   float* Xs_d = nullptr;         // prescaled/padded training inputs [n][DP]
   bool xs_dirty = true;
+  bool gram_ok = false;          // max_i |Xs_i|^2 <= kGramMaxSqNorm (Gram tile path allowed)
+  unsigned* sqnorm_d = nullptr;  // device word for that reduction
 
   int* err_d = nullptr;          // device error word
   int64_t launches = 0;          // kernels launched by this provider (diagnostics)

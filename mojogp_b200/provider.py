@@ -158,6 +158,14 @@ class Provider:
     def forward_matvec(self, out: DeviceBuffer, v: DeviceBuffer, ncols: int) -> None:
         _lib.call("gpb_forward_matvec", self.h, out.cptr, v.cptr, int(ncols))
 
+    LAYOUTS = {0: "scalar", 1: "ffma2", 2: "tensor-core", 3: "gram-tensor-core"}
+
+    def matvec_layout(self, ncols: int = 16) -> str:
+        """Name of the tile kernel the forward matvec uses for `ncols` columns."""
+        v = C.c_int32()
+        _lib.call("gpb_matvec_layout", self.h, int(ncols), C.byref(v))
+        return self.LAYOUTS[v.value]
+
     def forward_matvec_rows(self, out: DeviceBuffer, v: DeviceBuffer, ncols: int, r0: int,
                             r1: int) -> None:
         _lib.call("gpb_forward_matvec_rows", self.h, out.cptr, v.cptr, int(ncols), int(r0), int(r1))

@@ -1,0 +1,102 @@
+"""Gram-form tensor-core K·V path (both contractions on tcgen05) vs the fp64
+oracle at the 1e-5 relative-Frobenius matvec bar, plus the host's choice of
+path: taken for bounded prescaled norms and the leaves smooth in u at 0,
+refused for Matérn-1/2, the composite evaluator and large norms (where the
+difference-form kernels run and must still be exact to the same bar)."""
+import numpy as np
+import pytest
+
+from mojogp_b200.kernel import RBF, RQ, Matern12, Matern32, Matern52, make_ard_kernel
+from mojogp_b200.provider import DeviceBuffer, Provider
+from oracle import kernels as ok
+from tests.conftest import rel_fro
+
+pytestmark = pytest.mark.gpu
+
+LEAVES = {
+    "rbf_ard": lambda d: make_ard_kernel(RBF(ard=True), d),
+    "m32": lambda d: Matern32(),
+    "m52_ard": lambda d: make_ard_kernel(Matern52(ard=True), d),
+    "rq_ard": lambda d: make_ard_kernel(RQ(ard=True), d),
+}
+
+
+def _setup(kname, n, d, t, seed, ell=(0.5, 3.0), shift=0.0):
+    rng = np.random.default_rng(seed)
+    k = LEAVES[kname](d) if kname in LEAVES else kname
+    kk = k.resolve_ard(d)
+    names = kk.get_param_names()
+    p = np.empty(kk.num_params(), np.float32)
+    for i, nm in enumerate(names):
+        p[i] = rng.uniform(*ell) if ("length" in nm or "_ls_" in nm) else rng.uniform(0.5, 2.0)
+    X = (rng.standard_normal((n, d)) + shift).astype(np.float32)
+    V = rng.standard_normal((n, t)).astype(np.float32)
+    return k, p, X, V
+
+
+@pytest.mark.parametrize("kname", sorted(LEAVES))
+@pytest.mark.parametrize("n,d,t", [(5000, 16, 16), (1537, 16, 13), (700, 8, 16), (3000, 5, 32)])
+def test_gram_matvec_vs_oracle(gpb_lib, kname, n, d, t):
+    # Matérn prescaling multiplies by sqrt(3) or sqrt(5): longer lengthscales
+    # keep those inputs inside the norm bound too.
+    ell = (0.5, 3.0) if kname.startswith("rbf") or kname.startswith("rq") else (1.5, 3.0)
+    k, p, X, V = _setup(kname, n, d, t, seed=n + d + t, ell=ell)
+    prov = Provider(X, k, p, 0.1)
+    assert prov.matvec_layout(t) == "gram-tensor-core"
+    got = prov.matvec_host(V)
+    ref = ok.forward_matvec(k.to_spec(d), p, X, V, noise=0.1)
+    assert rel_fro(got, ref) < 1e-5
+
+
+def test_gram_refused_for_large_norms(gpb_lib):
+    # Shifted inputs with short lengthscales: max |x'|^2 far above the bound.
+    k, p, X, V = _setup("rbf_ard", 2000, 16, 16, seed=5, ell=(0.5, 0.8), shift=3.0)
+    prov = Provider(X, k, p, 0.1)
+    assert prov.matvec_layout(16) == "tensor-core"
+    ref = ok.forward_matvec(k.to_spec(16), p, X, V, noise=0.1)
+    assert rel_fro(prov.matvec_host(V), ref) < 1e-5
+
+
+@pytest.mark.parametrize("k", [Matern12(), RBF() + Matern52()])
+def test_gram_refused_for_other_kernels(gpb_lib, k):
+    rng = np.random.default_rng(2)
+    d = 16
+    X = rng.standard_normal((600, d)).astype(np.float32)
+    p = rng.uniform(0.5, 2.0, size=k.resolve_ard(d).num_params()).astype(np.float32)
+    prov = Provider(X, k, p, 0.1)
+    assert prov.matvec_layout(16) != "gram-tensor-core"
+
+
+def test_gram_param_update_rechecks_bound(gpb_lib):
+    # Shrinking the lengthscales raises the prescaled norms past the bound:
+    # the next matvec must leave the Gram path and stay exact.
+    k, p, X, V = _setup("rbf_ard", 1500, 16, 16, seed=9)
+    prov = Provider(X, k, p, 0.1)
+    assert prov.matvec_layout(16) == "gram-tensor-core"
+    p2 = p.copy()
+    names = k.resolve_ard(16).get_param_names()
+    for i, nm in enumerate(names):
+        if "length" in nm or "_ls_" in nm:
+            p2[i] = 0.2
+    prov.update_params(p2)
+    assert prov.matvec_layout(16) == "tensor-core"
+    ref = ok.forward_matvec(k.to_spec(16), p2, X, V, noise=0.1)
+    assert rel_fro(prov.matvec_host(V), ref) < 1e-5
+
+
+def test_gram_rows_and_cross(gpb_lib):
+    # Row-sharded output rows use the Gram path; the cross matvec (test rows
+    # with unchecked norms) uses the difference form. Both against the oracle.
+    k, p, X, V = _setup("rbf_ard", 2600, 16, 16, seed=4)
+    prov = Provider(X, k, p, 0.1)
+    full = prov.matvec_host(V)
+    vd = DeviceBuffer.from_host(np.ascontiguousarray(V.T))
+    od = DeviceBuffer((16, 1100))
+    prov.forward_matvec_rows(od, vd, 16, 700, 1800)
+    prov.synchronize()
+    assert rel_fro(od.download().T, full[700:1800]) < 1e-6
+    rng = np.random.default_rng(1)
+    Xt = rng.standard_normal((333, 16)).astype(np.float32)
+    got = prov.cross_matvec_host(Xt, V)
+    ref = ok.cross_matvec(k.to_spec(16), p, Xt, X, V)
+    assert rel_fro(got, ref) < 1e-5
