@@ -8,7 +8,8 @@ namespace gpb {
 // A [128][8] and B [16][8] (row = M or N index, 8 = K) in global memory;
 // D [128][16] out. `variant` 1 swaps the LBO / SBO roles (diagnostic);
 // `variant` 2 stages A in TMEM (tcgen05.st, one column per k) instead of
-// shared memory.
+// shared memory; `variant` 3 does the same with A left in full fp32 (the
+// tensor core reads the top 19 bits: truncation to tf32).
 __global__ void __launch_bounds__(128) tc_selftest_kernel(const float* __restrict__ A,
                                                           const float* __restrict__ B,
                                                           float* __restrict__ D, int variant,
@@ -38,9 +39,10 @@ __global__ void __launch_bounds__(128) tc_selftest_kernel(const float* __restric
   __syncthreads();
   tc_fence_after();
   const uint32_t taddr = tslot;
-  if (variant == 2) {
+  if (variant == 2 || variant == 3) {
     uint32_t r[8];
-    for (int k = 0; k < 8; ++k) r[k] = __float_as_uint(to_tf32(A[tid * 8 + k]));
+    for (int k = 0; k < 8; ++k)
+      r[k] = __float_as_uint(variant == 2 ? to_tf32(A[tid * 8 + k]) : A[tid * 8 + k]);
     tmem_st8(taddr + 32 + ((uint32_t)((tid / 32) * 32) << 16), r);
     tmem_wait_st();
     tc_fence_before();
