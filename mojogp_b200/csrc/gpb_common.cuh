@@ -94,13 +94,31 @@ __device__ __forceinline__ uint64_t global_timer_ns() {
   return t;
 }
 
-// Wait on an mbarrier phase for at most `limit_ns`; returns false on timeout.
+// try_wait with a suspend-time hint: the thread may sleep up to `hint_ns`
+// inside the instruction until the phase completes.
+__device__ __forceinline__ bool mbar_try_wait_hint(uint64_t* bar, uint32_t parity, uint32_t hint_ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_addr(bar)), "r"(parity), "r"(hint_ns)
+      : "memory");
+  return ok != 0;
+}
+
+// Wait on an mbarrier phase for at most about `limit_ns`; returns false on
+// timeout. The clock is read once per 32 polls, so a spinning thread costs
+// few issue slots.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity,
                                                   uint64_t limit_ns = 4000000000ull) {
   if (mbar_try_wait(bar, parity)) return true;
   const uint64_t t0 = global_timer_ns();
   while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
+#pragma unroll 1
+    for (int k = 0; k < 32; ++k)
+      if (mbar_try_wait(bar, parity)) return true;
     if (global_timer_ns() - t0 > limit_ns) return false;
   }
 }

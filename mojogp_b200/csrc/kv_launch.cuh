@@ -94,7 +94,7 @@ inline bool kv_uses_x2(int eval, int DP, int T) { return kv_layout(eval, DP, T) 
 // tile-blocked, 128 rows per tile, with the same average width).
 inline int kv_packed_width(int eval, int DP, int T, bool gram_ok = false) {
   switch (kv_layout(eval, DP, T, gram_ok)) {
-    case KV_GRAM: return 2 * DP + 1 + 32;
+    case KV_GRAM: return 2 * DP + 8 + 32;
     case KV_TC: return DP + 32;
     case KV_X2: return 2 * (DP + T);
     default: return ((DP + T) + 3) / 4 * 4;

@@ -179,7 +179,8 @@ int launch_pack_tc(const float* xs, int DP, float* v, int64_t v_ld, int c0, int 
   return GPB_OK;
 }
 
-// Gram tile packing: per 128 columns [-2y hi | -2y lo | |y|^2 | V hi | V lo]
+// Gram tile packing: per 128 columns [B hi | B lo | V hi | V lo] with
+// B = [-2y | 1 1 1 | |y|^2 in three exact tf32 parts | 0 0]
 // (kv_tiles_gram.cuh), with the same optional p = z + beta p update.
 __global__ void pack_gram_kernel(const float* __restrict__ xs, int DP, float* __restrict__ v,
                                  int64_t v_ld, int c0, int tcols, int64_t n, int64_t npad,
@@ -189,18 +190,23 @@ __global__ void pack_gram_kernel(const float* __restrict__ xs, int DP, float* __
   if (j >= npad) return;
   float* base = dst + (j / 128) * gram_tile_floats(DP);
   const int jt = (int)(j % 128);
+  const int KA = gram_kaug(DP);
   float y[32];
   for (int q = 0; q < DP; ++q) y[q] = (j < n) ? xs[j * DP + q] : 0.f;
   for (int q = 0; q < DP; ++q) {
     const float b = -2.f * y[q];
     const float hi = tf32_hi(b);
     base[gram_xoff(jt, q)] = hi;
-    base[128 * DP + gram_xoff(jt, q)] = b - hi;
+    base[128 * KA + gram_xoff(jt, q)] = b - hi;
   }
-  base[256 * DP + jt] = gram_sqnorm(y, DP);
-  float* bh = base + 256 * DP + 128 + (jt / 8) * 128;
-  float* bl = bh + 16 * 128;
+  float e[8] = {1.f, 1.f, 1.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  gram_split3(gram_sqnorm(y, DP), e[3], e[4], e[5]);
+  for (int q = 0; q < 8; ++q) base[gram_xoff(jt, DP + q)] = e[q];
+  // V block per 8-column k-step: N = 32 rows (n < 16: V hi, n >= 16: V lo),
+  // core matrices 8 n x 4 k, K-adjacent at 512 B, N-adjacent at 128 B.
+  float* vb = base + gram_v_offset(DP) + (jt / 8) * 256;
   const int k = jt % 8;
+  auto voff = [k](int nn) { return (k / 4) * 128 + (nn / 8) * 32 + (nn % 8) * 4 + (k % 4); };
   for (int c = 0; c < 16; ++c) {
     float val = 0.f;
     if (j < n && c < tcols) {
@@ -214,8 +220,8 @@ __global__ void pack_gram_kernel(const float* __restrict__ xs, int DP, float* __
       }
     }
     const float hi = tf32_hi(val);
-    bh[tc_b_offset(c, k)] = hi;
-    bl[tc_b_offset(c, k)] = val - hi;
+    vb[voff(c)] = hi;
+    vb[voff(16 + c)] = val - hi;
   }
 }
 
