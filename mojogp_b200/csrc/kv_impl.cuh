@@ -70,7 +70,7 @@ int kv_launch_tc(const KvLaunch& L) {
 template <int DP, int LEAF>
 int kv_launch_gram(const KvLaunch& L) {
   auto kern = kv_tile_gram_kernel<DP, LEAF>;
-  const size_t smem = ((size_t)kGStages * gram_tile_floats(DP) + (size_t)kGRowTiles * gram_a_floats(DP)) *
+  const size_t smem = ((size_t)kGStages * gram_tile_floats(DP)) *
                       sizeof(float);
   int dev = 0;
   GPB_CHECK_CUDA(cudaGetDevice(&dev));

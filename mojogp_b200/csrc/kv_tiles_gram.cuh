@@ -17,38 +17,65 @@
 // u at u = 0 (RBF, Matérn-3/2, Matérn-5/2, RQ); Matérn-1/2 (exp(-sqrt(u)))
 // keeps the difference form.
 //
-// CTA: 4 row tiles of 128 rows; warpgroup r (warps 4r..4r+3) owns row tile r
-// (TMEM lanes = rows), warp 16 + r issues its MMAs, warp 20 streams the
-// column tiles. Column tiles of 128 columns stream through a 3-deep TMA ring
-// and are consumed in chunks of 16 columns; per row tile the TMEM holds three
-// chunk stages of 32 columns ([16 cols: u, then K hi][16 cols: K lo]) and a
-// 32-column accumulator ([K V hi + K lo V hi | K hi V lo], summed at the end). tcgen05.mma instructions from one thread execute in
-// issue order, so MMA1 of chunk g+3 may overwrite the stage that MMA2 of chunk
-// g (issued before it) reads. Every wait is bounded.
+// CTA: 3 row tiles of 128 rows (TMEM lanes = rows); chunks of 16 columns.
+// Warpgroup r (warps 4r..4r+3) evaluates row tile r. A thread that issues an
+// MMA into an accumulator an earlier MMA of its own is still writing stalls
+// for that MMA's latency (~150 cycles), and one thread issues one MMA at a
+// time, so tensor throughput needs many issuing threads with independent
+// accumulators: per row tile one warp issues MMA1 of the even chunks, one of
+// the odd chunks, and likewise two warps issue MMA2 into an even and an odd
+// accumulator (summed at the end). The last warp streams column tiles through
+// a 4-deep TMA ring. Every A operand comes from TMEM (shared-memory A operands
+// of 4 KB per MMA would saturate shared memory).
+// TMEM columns: [x hi | x lo] per row tile, the norm k-step per row tile,
+// three chunk stages per row tile ([16: u, then K hi][16: K lo]) and two
+// 16-column accumulators per row tile. Every wait is bounded.
 #pragma once
 
 #include "kv_tiles_tc.cuh"
 
 namespace gpb {
 
-constexpr int kGRowTiles = 4;
+#ifdef GPB_GRAM_PROFILE
+// Diagnostic build only: cycles spent per role and wait, per translation unit.
+static __device__ unsigned long long g_gram_prof[16];
+#define GRAM_DECL long long gprof[8] = {0, 0, 0, 0, 0, 0, 0, 0}
+#define GRAM_T0(v) const long long v = clock64()
+#define GRAM_ACC(slot, t0) gprof[slot] += clock64() - (t0)
+#define GRAM_FLUSH                                                        \
+  if ((threadIdx.x & 31) == 0)                                            \
+    for (int q_ = 0; q_ < 8; ++q_)                                        \
+      if (gprof[q_]) atomicAdd(&g_gram_prof[q_], (unsigned long long)gprof[q_])
+#else
+#define GRAM_DECL
+#define GRAM_T0(v)
+#define GRAM_ACC(slot, t0)
+#define GRAM_FLUSH
+#endif
+
+constexpr int kGRowTiles = 3;
 constexpr int kGChunk = 16;
-constexpr int kGStages = 3;
+constexpr int kGStages = 4;    // column-tile ring depth (also keeps one CTA per SM)
+constexpr int kGUStages = 3;   // chunk stages in TMEM per row tile
 constexpr int kGEpiThreads = 128 * kGRowTiles;
-constexpr int kGThreads = kGEpiThreads + 32 * kGRowTiles + 32;
+constexpr int kGIssuerWarps = 4 * kGRowTiles;  // MMA1 even / odd, MMA2 even / odd
+constexpr int kGThreads = kGEpiThreads + 32 * kGIssuerWarps + 32;
 constexpr uint32_t kGTmemCols = 512;
-constexpr int kGD1Stages = 3;   // chunk stages in TMEM per row tile
-constexpr uint32_t kGAccCol = kGRowTiles * kGD1Stages * 32;
+// TMEM column map.
+constexpr uint32_t kGColX = 0;                                   // + 32 r : [x hi | x lo]
+constexpr uint32_t kGColN = kGColX + 32 * kGRowTiles;            // + 8 r  : norm k-step
+constexpr uint32_t kGColS = 128;                                 // + 96 r + 32 s : stage
+constexpr uint32_t kGColAcc = kGColS + 32 * kGUStages * kGRowTiles;  // + 32 r + 16 parity
+static_assert(kGColN + 8 * kGRowTiles <= kGColS, "TMEM map");
+static_assert(kGColAcc + 32 * kGRowTiles <= kGTmemCols, "TMEM budget");
 
 // Packed tile (floats): [B hi : 128 x (DP + 8)][B lo : 128 x DP]
 //                      [V : 16 k-steps x 256, N = 32 rows (V hi | V lo)]
-// with B = [-2y | 1 1 1 | |y|^2 parts | 0 0]; the row operand A (built by the
-// kernel) is [x | |x|^2 parts | 1 1 1 | 0 0].
+// with B = [-2y | 1 1 1 | |y|^2 parts | 0 0]; the row operand A is
+// [x | |x|^2 parts | 1 1 1 | 0 0], built in TMEM by the kernel.
 __host__ __device__ constexpr int gram_kaug(int DP) { return DP + 8; }
 __host__ __device__ constexpr int gram_tile_floats(int DP) { return 128 * (2 * DP + 8) + 4096; }
 __host__ __device__ constexpr int gram_v_offset(int DP) { return 128 * (2 * DP + 8); }
-// Per row tile: A hi [128 x (DP + 8)], A lo [128 x DP].
-__host__ __device__ constexpr int gram_a_floats(int DP) { return 128 * (2 * DP + 8); }
 
 // Offset (floats) of element (m, k) in a [128 x DP] K-major operand block:
 // 8-column k-steps of 1024 floats, core matrices of 8 rows x 4 k, K-adjacent
@@ -86,24 +113,19 @@ template <int DP, int LEAF>
 __global__ void __launch_bounds__(kGThreads, 1) kv_tile_gram_kernel(
     const float* __restrict__ xrow, int64_t nrow, const float* __restrict__ xv, int ntiles_total,
     int tiles_per_split, const __grid_constant__ FastParams fp, TileEpilogue ep, int* err) {
-  // Warps 0-15: four warpgroups, warpgroup r turns G into K hi/lo for row
-  // tile r (TMEM lanes = rows). Warps 16-19: issuer of row tile r's MMAs (one
-  // per SM sub-partition). Warp 20: streams column tiles into the ring; a slot
-  // is refilled once the four issuers' commits show every MMA reading it has
-  // completed. Hand-offs are mbarriers only.
-  static_assert(DP % 8 == 0, "K = DP in 8-wide tf32 k-steps");
+  static_assert(DP % 8 == 0 && DP <= 16, "K = DP in 8-wide tf32 k-steps, x hi / lo in 32 columns");
   constexpr int TILE = gram_tile_floats(DP);
   constexpr int kChunks = 128 / kGChunk;
-  constexpr int kIssuerWarp0 = kGEpiThreads / 32;
-  constexpr int kTmaWarp = kIssuerWarp0 + kGRowTiles;
+  constexpr int kIssuer0 = kGEpiThreads / 32;  // warp kIssuer0 + 4 r + role
+  constexpr int kTmaWarp = kIssuer0 + kGIssuerWarps;
   extern __shared__ __align__(1024) float smem[];
   float* ring_buf = smem;
-  float* a1 = smem + kGStages * TILE;  // per row tile: hi [128 x (DP+8)], lo [128 x DP]
-  __shared__ __align__(8) uint64_t full_bar[kGStages];                // TMA landed
-  __shared__ __align__(8) uint64_t tile_bar[kGStages];                // 4 issuers: slot done
-  __shared__ __align__(8) uint64_t d1_bar[kGRowTiles][kGD1Stages];    // G of a stage in TMEM
-  __shared__ __align__(8) uint64_t afull_bar[kGRowTiles][kGD1Stages]; // K hi/lo of a stage in TMEM
-  __shared__ __align__(8) uint64_t final_bar[kGRowTiles];
+  __shared__ __align__(8) uint64_t full_bar[kGStages];    // TMA landed
+  __shared__ __align__(8) uint64_t tile_bar[kGStages];    // MMAs reading the slot are done
+  __shared__ __align__(8) uint64_t d1_bar[kGRowTiles][kGUStages];     // MMA1 of a chunk done
+  __shared__ __align__(8) uint64_t afull_bar[kGRowTiles][kGUStages];  // K hi / lo in TMEM
+  __shared__ __align__(8) uint64_t m2_bar[kGRowTiles][kGUStages];     // MMA2 of a chunk done
+  __shared__ __align__(8) uint64_t final_bar;
   __shared__ uint32_t tslot;
 
   const int tid = threadIdx.x;
@@ -119,56 +141,65 @@ __global__ void __launch_bounds__(kGThreads, 1) kv_tile_gram_kernel(
       mbar_init(&full_bar[s], 1);
       mbar_init(&tile_bar[s], kGRowTiles);
     }
-    for (int r = 0; r < kGRowTiles; ++r) {
-      for (int s = 0; s < kGD1Stages; ++s) {
+    for (int r = 0; r < kGRowTiles; ++r)
+      for (int s = 0; s < kGUStages; ++s) {
         mbar_init(&d1_bar[r][s], 1);
         mbar_init(&afull_bar[r][s], 128);
+        mbar_init(&m2_bar[r][s], 1);
       }
-      mbar_init(&final_bar[r], 1);
-    }
+    mbar_init(&final_bar, 2 * kGRowTiles);
     fence_barrier_init();
   }
   if (warp == kTmaWarp) tmem_alloc(&tslot, kGTmemCols);
-
-  // Row operand: x_i split into tf32 hi / lo in the K-major layout, then
-  // the norm k-step [|x|^2 parts | 1 1 1 | 0 0] (hi only).
-  const int rt = tid / 128, m = tid % 128;
-  const int64_t i = (int64_t)blockIdx.x * kGEpiThreads + tid;
-  if (tid < kGEpiThreads) {
-    float x[DP];
-#pragma unroll
-    for (int k = 0; k < DP; ++k) x[k] = i < nrow ? xrow[i * DP + k] : 0.f;
-    float* ahi = a1 + rt * gram_a_floats(DP);
-    float* alo = ahi + 128 * gram_kaug(DP);
-#pragma unroll
-    for (int k = 0; k < DP; k += 4) {
-      float4 h, l;
-      h.x = tf32_hi(x[k]); l.x = x[k] - h.x;
-      h.y = tf32_hi(x[k + 1]); l.y = x[k + 1] - h.y;
-      h.z = tf32_hi(x[k + 2]); l.z = x[k + 2] - h.z;
-      h.w = tf32_hi(x[k + 3]); l.w = x[k + 3] - h.w;
-      *reinterpret_cast<float4*>(ahi + gram_xoff(m, k)) = h;
-      *reinterpret_cast<float4*>(alo + gram_xoff(m, k)) = l;
-    }
-    float4 e0, e1;
-    gram_split3(gram_sqnorm(x, DP), e0.x, e0.y, e0.z);
-    e0.w = 1.f;
-    e1 = make_float4(1.f, 1.f, 0.f, 0.f);
-    *reinterpret_cast<float4*>(ahi + gram_xoff(m, DP)) = e0;
-    *reinterpret_cast<float4*>(ahi + gram_xoff(m, DP + 4)) = e1;
-  }
   fence_proxy_async_smem();
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = tslot;
+  const int rt = tid / 128;
+  const int64_t i = (int64_t)blockIdx.x * kGEpiThreads + tid;
+  const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
+  if (tid < kGEpiThreads) {
+    // Row operand of row i (TMEM lane i % 128): x hi, x lo, norm k-step.
+    float x[DP];
+#pragma unroll
+    for (int k = 0; k < DP; ++k) x[k] = i < nrow ? xrow[i * DP + k] : 0.f;
+    const uint32_t a_row = tmem + lane_off + kGColX + rt * 32;
+#pragma unroll
+    for (int k8 = 0; k8 < DP; k8 += 8) {
+      uint32_t h[8], l[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const float hv = tf32_hi(x[k8 + k]);
+        h[k] = __float_as_uint(hv);
+        l[k] = __float_as_uint(x[k8 + k] - hv);
+      }
+      tmem_st8(a_row + k8, h);
+      tmem_st8(a_row + 16 + k8, l);
+    }
+    float e[8] = {0.f, 0.f, 0.f, 1.f, 1.f, 1.f, 0.f, 0.f};
+    gram_split3(gram_sqnorm(x, DP), e[0], e[1], e[2]);
+    uint32_t eb[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) eb[k] = __float_as_uint(e[k]);
+    tmem_st8(tmem + lane_off + kGColN + rt * 8, eb);
+    tmem_wait_st();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  GRAM_DECL;
+  auto off = [](int floats) -> uint64_t { return (uint64_t)((floats * 4) >> 4); };
+  const uint32_t idesc = make_idesc_tf32(128, 16);
 
   if (warp == kTmaWarp) {
     if (lane == 0) {
       bool ok = true;
       for (int kt = 0; kt < ntiles && ok; ++kt) {
         const int slot = kt % kGStages;
+        GRAM_T0(tw);
         if (kt >= kGStages) ok = mbar_wait_bounded(&tile_bar[slot], ((kt - kGStages) / kGStages) & 1);
+        GRAM_ACC(7, tw);
         if (!ok) break;
         mbar_arrive_expect_tx(&full_bar[slot], tile_bytes);
         bulk_copy_g2s(ring_buf + slot * TILE, xv + (int64_t)(t0 + kt) * TILE, tile_bytes,
@@ -177,83 +208,103 @@ __global__ void __launch_bounds__(kGThreads, 1) kv_tile_gram_kernel(
       if (!ok) atomicExch(err, DEV_WAIT_TIMEOUT);
     }
     __syncwarp();
-  } else if (warp >= kIssuerWarp0) {
-    const int r = warp - kIssuerWarp0;
-    if (lane == 0) {
-      const uint32_t idesc = make_idesc_tf32(128, 16);
-      const uint32_t d1_base = tmem + r * (kGD1Stages * 32);
-      const uint32_t acc_col = tmem + kGAccCol + r * 32;
-      const uint32_t idesc32 = make_idesc_tf32(128, 32);
-      // Descriptor bases; per-MMA offsets are added to the start-address field.
-      const float* ahi = a1 + r * gram_a_floats(DP);
-      const uint64_t dah0 = make_smem_desc(ahi, 2048, 128);
-      const uint64_t dal0 = make_smem_desc(ahi + 128 * gram_kaug(DP), 2048, 128);
+  } else if (warp >= kIssuer0) {
+    const int r = (warp - kIssuer0) / 4, role = (warp - kIssuer0) % 4;
+    const int par = role & 1;  // chunks c with c % 2 == par
+    if (lane == 0 && role < 2) {
+      // MMA1 of chunk c into stage c % 3 of row tile r, once MMA2 of chunk
+      // c - 3 (the stage's previous reader) has completed.
       const uint64_t dring0 = make_smem_desc(ring_buf, 2048, 128);
-      const uint64_t dv0 = make_smem_desc(ring_buf + gram_v_offset(DP), 512, 128);
-      auto off = [](int floats) -> uint64_t { return (uint64_t)((floats * 4) >> 4); };
-      auto issue_mma1 = [&](int c) -> bool {
+      const uint32_t ax = tmem + kGColX + r * 32, an = tmem + kGColN + r * 8;
+      bool ok = true;
+      GRAM_T0(itot);
+      for (int c = par; c < G && ok; c += 2) {
+        const int st = c % kGUStages;
         const int kt = c / kChunks, q = c % kChunks, slot = kt % kGStages;
-        if (q == 0) {
-          if (!mbar_wait_bounded(&full_bar[slot], (kt / kGStages) & 1)) return false;
-          tc_fence_after();
+        if (c >= kGUStages) {
+          GRAM_T0(mw);
+          ok = mbar_wait_bounded(&m2_bar[r][st], ((c - kGUStages) / kGUStages) & 1);
+          GRAM_ACC(4, mw);
+          if (!ok) break;
         }
+        if (q <= 1) {
+          GRAM_T0(fw);
+          ok = mbar_wait_bounded(&full_bar[slot], (kt / kGStages) & 1);
+          GRAM_ACC(5, fw);
+          if (!ok) break;
+        }
+        tc_fence_after();
         const uint64_t db = dring0 + off(slot * TILE + q * 64);
-        const uint32_t d = d1_base + (c % kGD1Stages) * 32;
+        const uint32_t d = tmem + kGColS + r * 96 + st * 32;
 #pragma unroll
         for (int ks = 0; ks < DP / 8; ++ks) {
-          mma_tf32(d, dah0 + off(ks * 1024), db + off(ks * 1024), idesc, ks > 0 ? 1u : 0u);
-          mma_tf32(d, dah0 + off(ks * 1024), db + off(128 * gram_kaug(DP) + ks * 1024), idesc, 1u);
-          mma_tf32(d, dal0 + off(ks * 1024), db + off(ks * 1024), idesc, 1u);
+          mma_tf32_tmem_a(d, ax + ks * 8, db + off(ks * 1024), idesc, ks > 0 ? 1u : 0u);
+          mma_tf32_tmem_a(d, ax + ks * 8, db + off(128 * gram_kaug(DP) + ks * 1024), idesc, 1u);
+          mma_tf32_tmem_a(d, ax + 16 + ks * 8, db + off(ks * 1024), idesc, 1u);
         }
         // Norm k-step: exact tf32 parts times exact ones, hi x hi only.
-        mma_tf32(d, dah0 + off(DP / 8 * 1024), db + off(DP / 8 * 1024), idesc, 1u);
-        mma_commit(&d1_bar[r][c % kGD1Stages]);
-        return true;
-      };
+        mma_tf32_tmem_a(d, an, db + off(DP / 8 * 1024), idesc, 1u);
+        mma_commit(&d1_bar[r][st]);
+      }
+      GRAM_ACC(3, itot);
+      if (!ok) atomicExch(err, DEV_WAIT_TIMEOUT);
+    } else if (lane == 0) {
+      // MMA2 of chunk c (c % 2 == par) into this warp's accumulator.
+      const uint64_t dv0 = make_smem_desc(ring_buf + gram_v_offset(DP), 512, 128);
+      const uint32_t acc = tmem + kGColAcc + r * 32 + par * 16;
       bool ok = true;
-      for (int c = 0; c < kGD1Stages && c < G && ok; ++c) ok = issue_mma1(c);
-      for (int g = 0; g < G && ok; ++g) {
-        const int st = g % kGD1Stages;
+      bool first = true;
+      GRAM_T0(itot);
+      for (int g = par; g < G && ok; g += 2) {
+        const int st = g % kGUStages;
         const int kt = g / kChunks, q = g % kChunks, slot = kt % kGStages;
-        ok = mbar_wait_bounded(&afull_bar[r][st], (g / kGD1Stages) & 1);
+        // V is read by this thread's MMAs: observe the TMA completion here too.
+        if (q <= 1) ok = mbar_wait_bounded(&full_bar[slot], (kt / kGStages) & 1);
+        if (!ok) break;
+        GRAM_T0(aw);
+        ok = mbar_wait_bounded(&afull_bar[r][st], (g / kGUStages) & 1);
+        GRAM_ACC(6, aw);
         if (!ok) break;
         tc_fence_after();
         const uint64_t dv = dv0 + off(slot * TILE + 2 * q * 256);
-        const uint32_t a = d1_base + st * 32;
-        // K hi x [V hi | V lo] (N = 32) and K lo x V hi (N = 16, first half).
+        const uint32_t a = tmem + kGColS + r * 96 + st * 32;
+        // K hi V hi + K hi V lo + K lo V hi (N = 16; V lo is the second half).
 #pragma unroll
         for (int kk = 0; kk < 2; ++kk) {
-          mma_tf32_tmem_a(acc_col, a + kk * 8, dv + off(kk * 256), idesc32, (g > 0 || kk > 0) ? 1u : 0u);
-          mma_tf32_tmem_a(acc_col, a + 16 + kk * 8, dv + off(kk * 256), idesc, 1u);
+          mma_tf32_tmem_a(acc, a + kk * 8, dv + off(kk * 256), idesc, (first && kk == 0) ? 0u : 1u);
+          mma_tf32_tmem_a(acc, a + kk * 8, dv + off(kk * 256 + 64), idesc, 1u);
+          mma_tf32_tmem_a(acc, a + 16 + kk * 8, dv + off(kk * 256), idesc, 1u);
         }
+        first = false;
+        mma_commit(&m2_bar[r][st]);
         if (q == kChunks - 1) mma_commit(&tile_bar[slot]);
-        if (g + kGD1Stages < G) ok = issue_mma1(g + kGD1Stages);
       }
-      mma_commit(&final_bar[r]);
+      GRAM_ACC(2, itot);
+      mma_commit(&final_bar);
       if (!ok) atomicExch(err, DEV_WAIT_TIMEOUT);
-      // No MMA of this row tile may still be in flight when TMEM is released.
-      mbar_wait_bounded(&final_bar[r], 0);
+      // No MMA of this thread may still be in flight when TMEM is released.
+      mbar_wait_bounded(&final_bar, 0);
     }
     __syncwarp();
   } else {
-    const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
-    const uint32_t d1_base = tmem + rt * (kGD1Stages * 32);
-    const uint32_t acc_col = tmem + kGAccCol + rt * 32;
+    const uint32_t s_base = tmem + lane_off + kGColS + rt * 96;
+    const uint32_t acc_col = tmem + lane_off + kGColAcc + rt * 32;
     bool ok = true;
-    // Software pipeline: the TMEM load of chunk g+1 is in flight while chunk
-    // g is evaluated. Two register buffers alternate (loop unrolled by two).
-    auto fetch = [&](int c, uint32_t (&raw)[16]) -> bool {
-      if (!mbar_wait_bounded(&d1_bar[rt][c % kGD1Stages], (c / kGD1Stages) & 1)) return false;
+    GRAM_T0(etot);
+    for (int g = 0; g < G && ok; ++g) {
+      const int st = g % kGUStages;
+      GRAM_T0(dw);
+      ok = mbar_wait_bounded(&d1_bar[rt][st], (g / kGUStages) & 1);
+      GRAM_ACC(0, dw);
+      if (!ok) break;
       tc_fence_after();
-      tmem_ld16_async(d1_base + lane_off + (c % kGD1Stages) * 32, raw);
-      return true;
-    };
-    auto process = [&](int c, const uint32_t (&raw)[16]) {
-      const uint32_t taddr = d1_base + lane_off + (c % kGD1Stages) * 32;
+      const uint32_t taddr = s_base + st * 32;
+      float u[16];
+      tmem_ld16(taddr, u);  // includes tcgen05.wait::ld
       uint32_t hi[16], lo[16];
 #pragma unroll
       for (int h = 0; h < 16; ++h) {
-        const float kv = FastEval<LEAF>::value(__uint_as_float(raw[h]), fp);
+        const float kv = FastEval<LEAF>::value(u[h], fp);
         // The tensor core reads the top 19 bits of each 32-bit A element
         // (tf32 truncation), so k itself serves as the hi part and the lo
         // part is k minus its truncation.
@@ -264,33 +315,23 @@ __global__ void __launch_bounds__(kGThreads, 1) kv_tile_gram_kernel(
       tmem_st16(taddr + 16, lo);
       tmem_wait_st();
       tc_fence_before();
-      mbar_arrive(&afull_bar[rt][c % kGD1Stages]);
-    };
-    uint32_t rawA[16], rawB[16];
-    if (G > 0) ok = fetch(0, rawA);
-    for (int g = 0; g < G && ok; g += 2) {
-      tmem_wait_ld();
-      if (g + 1 < G) ok = fetch(g + 1, rawB);
-      if (!ok) break;
-      process(g, rawA);
-      if (g + 1 >= G) break;
-      tmem_wait_ld();
-      if (g + 2 < G) ok = fetch(g + 2, rawA);
-      if (!ok) break;
-      process(g + 1, rawB);
+      mbar_arrive(&afull_bar[rt][st]);
     }
-    if (ok) ok = mbar_wait_bounded(&final_bar[rt], 0);
+    GRAM_ACC(1, etot);
+    if (ok) ok = mbar_wait_bounded(&final_bar, 0);
     tc_fence_after();
     if (!ok) {
       atomicExch(err, DEV_WAIT_TIMEOUT);
     } else {
       float acc[16];
       if (G > 0) {
-        float acc_lo[16];
-        tmem_ld16(acc_col + lane_off, acc);
-        tmem_ld16(acc_col + lane_off + 16, acc_lo);
+        tmem_ld16(acc_col, acc);  // even chunks
+        if (G > 1) {
+          float acc_odd[16];
+          tmem_ld16(acc_col + 16, acc_odd);
 #pragma unroll
-        for (int c = 0; c < 16; ++c) acc[c] += acc_lo[c];
+          for (int c = 0; c < 16; ++c) acc[c] += acc_odd[c];
+        }
       } else {
 #pragma unroll
         for (int c = 0; c < 16; ++c) acc[c] = 0.f;
@@ -314,6 +355,7 @@ __global__ void __launch_bounds__(kGThreads, 1) kv_tile_gram_kernel(
       }
     }
   }
+  GRAM_FLUSH;
   tc_fence_before();
   __syncthreads();
   if (warp == kTmaWarp) tmem_dealloc(tmem, kGTmemCols);
