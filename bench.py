@@ -31,6 +31,11 @@ sys.path.insert(0, str(ROOT))
 METRIC = "kernel-matvec TFLOP/s & fit s/iter at n=1M,d=16,t=16"
 UNIT = "TFLOP/s"
 F_PER_PAIR_RBF = lambda d, t: 3 * d + 3 + 2 * t  # algorithmic flops per kernel entry
+# Tensor-core flops the Gram-form kernel issues per kernel entry (d padded to
+# DP = 16): MMA1 3xTF32 on x·y (3 * 2 * DP) + the norm k-step (2 * 8), MMA2
+# three tf32 products into t = 16 columns (3 * 2 * t).
+TC_PER_PAIR_GRAM = lambda dp, t: 3 * 2 * dp + 2 * 8 + 3 * 2 * t
+MUFU_PER_SM_CLK = 16  # MUFU (ex2) results per SM per clock on B200: 4 per sub-partition
 
 
 def parse():
@@ -225,22 +230,44 @@ def main():
                        "iterations = max_tridiag, SLQ, fused gradients, Adam)"}
 
     achieved = flops_local / (kmean * 1e-3) / 1e12
+    layout = prov.matvec_layout(t)
+    pairs_per_s = float(r1 - r0) * n / (kmean * 1e-3)
+    sm_mhz = (clocks or {}).get("sm_mhz") or 1965.0
+    fp32_peak = {"achieved": achieved, "peak": peak_tf.value, "unit": "TFLOP/s",
+                 "frac": achieved / peak_tf.value, "flops_per_pair": F,
+                 "peak_source": "measured FFMA probe (gpb_measure_fp32_peak) on this GPU"}
+    if layout == "gram-tensor-core":
+        peaks_path = Path(__file__).resolve().parent / "MEASURED_PEAKS.json"
+        try:
+            bf16 = float(json.loads(peaks_path.read_text())["bf16_tflops"])
+            src = "of measured: MEASURED_PEAKS.json bf16_tflops (burst) / 2 = dense tf32"
+        except (OSError, KeyError, ValueError):
+            bf16, src = 1590.0, "of fallback: 1.59 PFLOP/s bf16 / 2 = dense tf32"
+        dp = 16 if d > 8 else 8
+        tc = TC_PER_PAIR_GRAM(dp, 16)
+        tc_achieved = pairs_per_s * tc / 1e12
+        roofline = {"bound": "tensor", "achieved": tc_achieved, "peak": bf16 / 2,
+                    "unit": "TFLOP/s", "frac": tc_achieved / (bf16 / 2), "traffic": None,
+                    "peak_source": src, "tensor_flops_per_pair": tc,
+                    "mufu": {"achieved_per_sm_clk": pairs_per_s / 148 / (sm_mhz * 1e6),
+                             "peak_per_sm_clk": MUFU_PER_SM_CLK,
+                             "frac": pairs_per_s / 148 / (sm_mhz * 1e6) / MUFU_PER_SM_CLK},
+                    "fp32_equivalent": fp32_peak}
+    else:
+        roofline = dict(bound="fp32", traffic=None,
+                        nominal_peak=148 * 128 * 2 * 1.965e9 / 1e12, **fp32_peak)
     line = {
         "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": steps,
         "warmup": warm, "ms_per_step": total_ms / steps, "higher_is_better": True,
         "scaling": "strong", "vs_baseline": None, "dtype": "f32",
         "data": "synthetic (config 3 recipe: X~N(0,I), l~U[0.5,3], seed 3)",
         "config": {"workload": "config3 K(X,X)V RBF-ARD matrix-free, t=16", "n": n, "d": d,
-                   "t": t, "parallelism": f"row-shard x{world}",
+                   "t": t, "parallelism": f"row-shard x{world}", "tile_kernel": layout,
                    "l2": "256 MB flush before every step; packed column tiles 128 MB"},
         "gpu_launches": int(launches.sum()),
         "e2e": {"value": e2e_tf, "unit": UNIT, "h2d_bytes_per_step": int(Vc.nbytes),
                 "d2h_bytes_per_step": int(Vc.nbytes)},
-        "roofline": {"bound": "fp32", "achieved": achieved, "peak": peak_tf.value,
-                     "unit": "TFLOP/s", "frac": achieved / peak_tf.value, "traffic": None,
-                     "peak_source": "measured FFMA probe (gpb_measure_fp32_peak) on this GPU",
-                     "nominal_peak": 148 * 128 * 2 * 1.965e9 / 1e12,
-                     "flops_per_pair": F},
+        "roofline": roofline,
         "clocks": clocks,
         "fit": fit,
     }

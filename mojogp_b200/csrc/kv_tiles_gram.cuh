@@ -4,7 +4,7 @@
 //   MMA1  u = [x_i | |x_i|^2 parts | 1 1 1] · [-2 y_j | 1 1 1 | |y_j|^2 parts]
 //           = |x_i|^2 + |y_j|^2 - 2 x_i·y_j       (3xTF32 on the x·y block)
 //   k_ij  = leaf(u_ij), split into tf32 hi / lo   (CUDA cores)   -> TMEM
-//   MMA2  D += K_hi [V_hi | V_lo] + K_lo V_hi     (A from TMEM)  -> TMEM
+//   MMA2  D += K_hi V_hi + K_hi V_lo + K_lo V_hi  (A from TMEM)  -> TMEM
 // The squared norms ride along as one extra 8-wide k-step: each norm is split
 // into three tf32 parts that sum to it exactly, multiplied by exact ones, so
 // that k-step needs only the hi x hi product. The CUDA cores are left with the
@@ -53,21 +53,30 @@ static __device__ unsigned long long g_gram_prof[16];
 #define GRAM_FLUSH
 #endif
 
-constexpr int kGRowTiles = 3;
+#ifndef GPB_GRAM_R
+#define GPB_GRAM_R 3
+#endif
+#ifndef GPB_GRAM_S
+#define GPB_GRAM_S 3
+#endif
+#ifndef GPB_GRAM_P
+#define GPB_GRAM_P 2
+#endif
+constexpr int kGRowTiles = GPB_GRAM_R;
 constexpr int kGChunk = 16;
 constexpr int kGStages = 4;    // column-tile ring depth (also keeps one CTA per SM)
-constexpr int kGUStages = 3;   // chunk stages in TMEM per row tile
+constexpr int kGUStages = GPB_GRAM_S;  // chunk stages in TMEM per row tile
+constexpr int kGPar = GPB_GRAM_P;      // issuer warps per role and row tile (chunk c -> c % kGPar)
 constexpr int kGEpiThreads = 128 * kGRowTiles;
-constexpr int kGIssuerWarps = 4 * kGRowTiles;  // MMA1 even / odd, MMA2 even / odd
+constexpr int kGIssuerWarps = 2 * kGPar * kGRowTiles;  // MMA1 and MMA2 issuers
 constexpr int kGThreads = kGEpiThreads + 32 * kGIssuerWarps + 32;
 constexpr uint32_t kGTmemCols = 512;
 // TMEM column map.
 constexpr uint32_t kGColX = 0;                                   // + 32 r : [x hi | x lo]
 constexpr uint32_t kGColN = kGColX + 32 * kGRowTiles;            // + 8 r  : norm k-step
-constexpr uint32_t kGColS = 128;                                 // + 96 r + 32 s : stage
-constexpr uint32_t kGColAcc = kGColS + 32 * kGUStages * kGRowTiles;  // + 32 r + 16 parity
-static_assert(kGColN + 8 * kGRowTiles <= kGColS, "TMEM map");
-static_assert(kGColAcc + 32 * kGRowTiles <= kGTmemCols, "TMEM budget");
+constexpr uint32_t kGColS = (40 * kGRowTiles + 31) / 32 * 32;     // + 32 S r + 32 s : stage
+constexpr uint32_t kGColAcc = kGColS + 32 * kGUStages * kGRowTiles;  // + 16 P r + 16 class
+static_assert(kGColAcc + 16 * kGPar * kGRowTiles <= kGTmemCols, "TMEM budget");
 
 // Packed tile (floats): [B hi : 128 x (DP + 8)][B lo : 128 x DP]
 //                      [V : 16 k-steps x 256, N = 32 rows (V hi | V lo)]
@@ -116,7 +125,7 @@ __global__ void __launch_bounds__(kGThreads, 1) kv_tile_gram_kernel(
   static_assert(DP % 8 == 0 && DP <= 16, "K = DP in 8-wide tf32 k-steps, x hi / lo in 32 columns");
   constexpr int TILE = gram_tile_floats(DP);
   constexpr int kChunks = 128 / kGChunk;
-  constexpr int kIssuer0 = kGEpiThreads / 32;  // warp kIssuer0 + 4 r + role
+  constexpr int kIssuer0 = kGEpiThreads / 32;  // warp kIssuer0 + 2 P r + role
   constexpr int kTmaWarp = kIssuer0 + kGIssuerWarps;
   extern __shared__ __align__(1024) float smem[];
   float* ring_buf = smem;
@@ -147,7 +156,7 @@ __global__ void __launch_bounds__(kGThreads, 1) kv_tile_gram_kernel(
         mbar_init(&afull_bar[r][s], 128);
         mbar_init(&m2_bar[r][s], 1);
       }
-    mbar_init(&final_bar, 2 * kGRowTiles);
+    mbar_init(&final_bar, kGPar * kGRowTiles);
     fence_barrier_init();
   }
   if (warp == kTmaWarp) tmem_alloc(&tslot, kGTmemCols);
@@ -209,16 +218,16 @@ __global__ void __launch_bounds__(kGThreads, 1) kv_tile_gram_kernel(
     }
     __syncwarp();
   } else if (warp >= kIssuer0) {
-    const int r = (warp - kIssuer0) / 4, role = (warp - kIssuer0) % 4;
-    const int par = role & 1;  // chunks c with c % 2 == par
-    if (lane == 0 && role < 2) {
+    const int r = (warp - kIssuer0) / (2 * kGPar), role = (warp - kIssuer0) % (2 * kGPar);
+    const int par = role % kGPar;  // chunks c with c % kGPar == par
+    if (lane == 0 && role < kGPar) {
       // MMA1 of chunk c into stage c % 3 of row tile r, once MMA2 of chunk
       // c - 3 (the stage's previous reader) has completed.
       const uint64_t dring0 = make_smem_desc(ring_buf, 2048, 128);
       const uint32_t ax = tmem + kGColX + r * 32, an = tmem + kGColN + r * 8;
       bool ok = true;
       GRAM_T0(itot);
-      for (int c = par; c < G && ok; c += 2) {
+      for (int c = par; c < G && ok; c += kGPar) {
         const int st = c % kGUStages;
         const int kt = c / kChunks, q = c % kChunks, slot = kt % kGStages;
         if (c >= kGUStages) {
@@ -227,7 +236,7 @@ __global__ void __launch_bounds__(kGThreads, 1) kv_tile_gram_kernel(
           GRAM_ACC(4, mw);
           if (!ok) break;
         }
-        if (q <= 1) {
+        if (q < kGPar) {
           GRAM_T0(fw);
           ok = mbar_wait_bounded(&full_bar[slot], (kt / kGStages) & 1);
           GRAM_ACC(5, fw);
@@ -235,7 +244,7 @@ __global__ void __launch_bounds__(kGThreads, 1) kv_tile_gram_kernel(
         }
         tc_fence_after();
         const uint64_t db = dring0 + off(slot * TILE + q * 64);
-        const uint32_t d = tmem + kGColS + r * 96 + st * 32;
+        const uint32_t d = tmem + kGColS + r * 32 * kGUStages + st * 32;
 #pragma unroll
         for (int ks = 0; ks < DP / 8; ++ks) {
           mma_tf32_tmem_a(d, ax + ks * 8, db + off(ks * 1024), idesc, ks > 0 ? 1u : 0u);
@@ -251,15 +260,15 @@ __global__ void __launch_bounds__(kGThreads, 1) kv_tile_gram_kernel(
     } else if (lane == 0) {
       // MMA2 of chunk c (c % 2 == par) into this warp's accumulator.
       const uint64_t dv0 = make_smem_desc(ring_buf + gram_v_offset(DP), 512, 128);
-      const uint32_t acc = tmem + kGColAcc + r * 32 + par * 16;
+      const uint32_t acc = tmem + kGColAcc + r * 16 * kGPar + par * 16;
       bool ok = true;
       bool first = true;
       GRAM_T0(itot);
-      for (int g = par; g < G && ok; g += 2) {
+      for (int g = par; g < G && ok; g += kGPar) {
         const int st = g % kGUStages;
         const int kt = g / kChunks, q = g % kChunks, slot = kt % kGStages;
         // V is read by this thread's MMAs: observe the TMA completion here too.
-        if (q <= 1) ok = mbar_wait_bounded(&full_bar[slot], (kt / kGStages) & 1);
+        if (q < kGPar) ok = mbar_wait_bounded(&full_bar[slot], (kt / kGStages) & 1);
         if (!ok) break;
         GRAM_T0(aw);
         ok = mbar_wait_bounded(&afull_bar[r][st], (g / kGUStages) & 1);
@@ -267,7 +276,7 @@ __global__ void __launch_bounds__(kGThreads, 1) kv_tile_gram_kernel(
         if (!ok) break;
         tc_fence_after();
         const uint64_t dv = dv0 + off(slot * TILE + 2 * q * 256);
-        const uint32_t a = tmem + kGColS + r * 96 + st * 32;
+        const uint32_t a = tmem + kGColS + r * 32 * kGUStages + st * 32;
         // K hi V hi + K hi V lo + K lo V hi (N = 16; V lo is the second half).
 #pragma unroll
         for (int kk = 0; kk < 2; ++kk) {
@@ -287,8 +296,8 @@ __global__ void __launch_bounds__(kGThreads, 1) kv_tile_gram_kernel(
     }
     __syncwarp();
   } else {
-    const uint32_t s_base = tmem + lane_off + kGColS + rt * 96;
-    const uint32_t acc_col = tmem + lane_off + kGColAcc + rt * 32;
+    const uint32_t s_base = tmem + lane_off + kGColS + rt * 32 * kGUStages;
+    const uint32_t acc_col = tmem + lane_off + kGColAcc + rt * 16 * kGPar;
     bool ok = true;
     GRAM_T0(etot);
     for (int g = 0; g < G && ok; ++g) {
@@ -325,12 +334,12 @@ __global__ void __launch_bounds__(kGThreads, 1) kv_tile_gram_kernel(
     } else {
       float acc[16];
       if (G > 0) {
-        tmem_ld16(acc_col, acc);  // even chunks
-        if (G > 1) {
-          float acc_odd[16];
-          tmem_ld16(acc_col + 16, acc_odd);
+        tmem_ld16(acc_col, acc);  // chunk class 0
+        for (int p = 1; p < kGPar && p < G; ++p) {
+          float acc_p[16];
+          tmem_ld16(acc_col + 16 * p, acc_p);
 #pragma unroll
-          for (int c = 0; c < 16; ++c) acc[c] += acc_odd[c];
+          for (int c = 0; c < 16; ++c) acc[c] += acc_p[c];
         }
       } else {
 #pragma unroll
