@@ -312,6 +312,20 @@ int gpb_lmc_bbmm(gpb_lmc* h, const float* y_centered_host, int32_t num_probes, i
                  double* nll_out, double* kernel_grads_out, double* grad_A_out,
                  double* grad_noise_out, double* sum_alpha_out, float* alpha_out,
                  int32_t* cg_iters_out);
+/* Sum-of-Kronecker Woodbury preconditioner (lmc_preconditioner.mojo:143-470,
+ * built as in jit_lmc.mojo:848-900): P = sum_s A_s (x) L_s L_s^T + D with L_s
+ * the rank-`rank` pivoted-Cholesky factor of K_s, from the current A_s and
+ * noise. Once built, gpb_lmc_bbmm preconditions with it (probes ~ N(0, P),
+ * log|P| added) until rebuilt; rank <= 0 removes it. ranks_out [R] (actual
+ * per-latent ranks) and logdet_out (log|P|) may be NULL. */
+int gpb_lmc_build_precond(gpb_lmc* h, int32_t rank, int32_t* ranks_out, double* logdet_out);
+/* out = P^{-1} v for ncols task-blocked device columns (apply_precond,
+ * lmc_preconditioner.mojo:397-560). */
+int gpb_lmc_precond_apply(gpb_lmc* h, float* out_dev, const float* v_dev, int64_t ncols);
+/* num probes ~ N(0, P): D^{1/2} eps + U omega with counter-hash Gaussians
+ * (omega seed `seed`, eps seed `seed + 1e6`) in place of the reference's host
+ * generator (sample_probes, lmc_preconditioner.mojo:567-719). */
+int gpb_lmc_precond_sample(gpb_lmc* h, float* out_dev, int32_t num, uint64_t seed);
 /* K_full^{-1} rhs by CG (relative-residual stop), rhs and x [T*n] host. */
 int gpb_lmc_solve(gpb_lmc* h, const float* rhs_host, int32_t max_cg_iter, float cg_tol,
                   float* x_host_out, int32_t* iters_out);

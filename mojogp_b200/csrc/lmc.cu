@@ -39,6 +39,159 @@ __global__ void lmc_mix_kernel(float* __restrict__ out, const float* __restrict_
   out[idx] = s;
 }
 
+// ---------------------------------------------------------- preconditioner
+// Sum-of-Kronecker Woodbury preconditioner (kernels/lmc_preconditioner.mojo:
+// 143-470, built as in jit_lmc.mojo:848-900, 1047-1100):
+//   P = sum_s (C_s (x) L_s)(C_s (x) L_s)^T + D = sum_s A_s (x) L_s L_s^T + D,
+// with L_s the rank-r_s greedy pivoted-Cholesky factor of K_s (no noise),
+// C_s = chol(A_s) and D = diag(noise_t (x) 1_n). With U = [C_s (x) L_s]_s and
+// M = I + U^T D^{-1} U (order (s, j, k) -> off_s + j r_s + k):
+//   P^{-1} v = D^{-1} v - D^{-1} U M^{-1} U^T D^{-1} v,
+//   log|P|   = n sum_t log noise_t + log|M|,
+//   z ~ N(0, P): z = D^{1/2} eps + U omega.
+// B200 changes: M^{-1} (fp64) lives on the device and every step of an apply
+// is a batched kernel over all columns, latents and tasks (no host round trip
+// per column / latent / task); probes use the library's counter-hash Gaussian
+// (seeds `seed` for omega, `seed + 1e6` for eps) instead of a host generator.
+// y_s[j][k] = sum_t C_s[t][j] Z_s[c][t][k]; z = Minv y; u_s[c][t][k] = scale_t *
+// sum_j C_s[t][j] z_s[j][k]. One block per column c. With `omega` set, z is
+// read from omega[c][Kt] instead (probe sampling: no Z, no Minv).
+__global__ void lmc_pc_small_kernel(const double* __restrict__ Z, const float* __restrict__ C,
+                                    const double* __restrict__ Minv, const float* __restrict__ omega,
+                                    const int* __restrict__ rank, const int* __restrict__ off,
+                                    int R, int T, int Kt, const float* __restrict__ scale,
+                                    float* __restrict__ u) {
+  extern __shared__ double sh[];
+  double* y = sh;
+  double* z = sh + Kt;
+  const int c = blockIdx.x;
+  // Z and u: latent s occupies [cols * T][r_s] starting at off_s * cols.
+  const int cols = gridDim.x;
+  if (omega) {
+    for (int q = threadIdx.x; q < Kt; q += blockDim.x) z[q] = omega[(int64_t)c * Kt + q];
+  } else {
+    for (int q = threadIdx.x; q < Kt; q += blockDim.x) {
+      int s = 0;
+      while (s + 1 < R && off[s + 1] <= q) ++s;
+      const int rs = rank[s], loc = q - off[s];
+      const int j = loc / rs, k = loc % rs;
+      const double* Zs = Z + (int64_t)off[s] * cols;
+      double acc = 0.0;
+      for (int t = 0; t < T; ++t)
+        acc += (double)C[((size_t)s * T + t) * T + j] * Zs[((int64_t)c * T + t) * rs + k];
+      y[q] = acc;
+    }
+    __syncthreads();
+    for (int q = threadIdx.x; q < Kt; q += blockDim.x) {
+      double acc = 0.0;
+      const double* row = Minv + (int64_t)q * Kt;
+      for (int q2 = 0; q2 < Kt; ++q2) acc += row[q2] * y[q2];
+      z[q] = acc;
+    }
+  }
+  __syncthreads();
+  // u_s laid out like Z_s: u[(off_s * cols) + (c * T + t) * r_s + k].
+  for (int q = threadIdx.x; q < Kt; q += blockDim.x) {
+    int s = 0;
+    while (s + 1 < R && off[s + 1] <= q) ++s;
+    const int rs = rank[s], loc = q - off[s];
+    const int t = loc / rs, k = loc % rs;  // reuse (j, k) indexing with j -> t
+    double acc = 0.0;
+    for (int j = 0; j < T; ++j)
+      acc += (double)C[((size_t)s * T + t) * T + j] * z[off[s] + j * rs + k];
+    u[(int64_t)off[s] * cols + ((int64_t)c * T + t) * rs + k] = (float)(scale[t] * acc);
+  }
+}
+
+// out[c][t][i] = scale[t] * v[c][t][i]
+__global__ void lmc_task_scale_kernel(float* __restrict__ out, const float* __restrict__ v,
+                                      const float* __restrict__ scale, int T, int64_t n,
+                                      int64_t total) {
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (idx >= total) return;
+  const int t = (int)((idx / n) % T);
+  out[idx] = scale[t] * v[idx];
+}
+
+struct LmcPrecond {
+  int R = 0, T = 0, Kt = 0;
+  int64_t n = 0;
+  std::vector<int> rank, off;       // per latent
+  std::vector<Precond> pc;          // per latent: L_s
+  std::vector<float> C;             // [R][T][T] row-major lower Cholesky of A_s
+  std::vector<float> noise;         // [T]
+  double logdet = 0.0;
+  DBuf C_d, dinv_d, dsqrt_d, ones_d, Minv_d, rank_d, off_d, Z_d, u_d, w_d, omega_d;
+  // Columns per batched pass: L^T v shared memory (t (128 + r) floats) and
+  // L u shared memory (t r floats, 48 KB default) bound it.
+  int group_cols(int cols) const {
+    int rmax = 1;
+    for (int r : rank) rmax = std::max(rmax, r);
+    int g = std::min(190 * 1024 / (4 * T * (128 + rmax)), 12000 / (T * rmax));
+    return std::max(1, std::min(cols, g));
+  }
+};
+
+int lmc_precond_apply(Engine& E, LmcPrecond& P, const float* v, float* out, int t) {
+  const int64_t nT = (int64_t)P.T * P.n, cnt = (int64_t)t * nT;
+  cudaStream_t st = E.st;
+  GPB_TRY(P.w_d.ensure((size_t)cnt * sizeof(float)));
+  float* w = P.w_d.f();
+  lmc_task_scale_kernel<<<(unsigned)ceil_div(cnt, 256), 256, 0, st>>>(w, v, P.dinv_d.f(), P.T, P.n,
+                                                                     cnt);
+  GPB_CHECK_CUDA(cudaGetLastError());
+  const int gmax = P.group_cols(t);
+  GPB_TRY(P.Z_d.ensure((size_t)gmax * P.Kt * sizeof(double)));
+  GPB_TRY(P.u_d.ensure((size_t)gmax * P.Kt * sizeof(float)));
+  for (int c0 = 0; c0 < t; c0 += gmax) {
+    const int g = std::min(gmax, t - c0);
+    const float* wg = w + (int64_t)c0 * nT;
+    float* og = out + (int64_t)c0 * nT;
+    for (int s = 0; s < P.R; ++s) {
+      GPB_TRY(k_ltv(P.pc[s].L.f(), P.n, P.rank[s], wg, P.n, g * P.T, E.red, st));
+      GPB_CHECK_CUDA(cudaMemcpyAsync(P.Z_d.d() + (int64_t)P.off[s] * g, E.red.sums.ptr,
+                                     (size_t)g * P.T * P.rank[s] * sizeof(double),
+                                     cudaMemcpyDeviceToDevice, st));
+    }
+    lmc_pc_small_kernel<<<g, 256, 2 * (size_t)P.Kt * sizeof(double), st>>>(
+        P.Z_d.d(), P.C_d.f(), P.Minv_d.d(), nullptr, (const int*)P.rank_d.ptr,
+        (const int*)P.off_d.ptr, P.R, P.T, P.Kt, P.dinv_d.f(), P.u_d.f());
+    GPB_CHECK_CUDA(cudaGetLastError());
+    for (int s = 0; s < P.R; ++s)
+      GPB_TRY(k_l_times_u(P.pc[s].L.f(), P.n, P.rank[s], P.u_d.f() + (int64_t)P.off[s] * g,
+                          g * P.T, s == 0 ? wg : og, P.n, 1.f, -1.f, og, st));
+  }
+  E.p->launches += 1 + (int64_t)((t + gmax - 1) / gmax) * (2 * P.R + 1);
+  return GPB_OK;
+}
+
+int lmc_precond_sample(Engine& E, LmcPrecond& P, int num, uint64_t seed, float* out) {
+  const int64_t nT = (int64_t)P.T * P.n, cnt = (int64_t)num * nT;
+  cudaStream_t st = E.st;
+  GPB_TRY(k_gaussian(out, num, nT, nT, nT, 0, seed + 1000000ull, st));
+  lmc_task_scale_kernel<<<(unsigned)ceil_div(cnt, 256), 256, 0, st>>>(out, out, P.dsqrt_d.f(), P.T,
+                                                                     P.n, cnt);
+  GPB_CHECK_CUDA(cudaGetLastError());
+  GPB_TRY(P.omega_d.ensure((size_t)num * P.Kt * sizeof(float)));
+  const int64_t no = (int64_t)num * P.Kt;
+  GPB_TRY(k_gaussian(P.omega_d.f(), 1, no, no, no, 0, seed, st));
+  const int gmax = P.group_cols(num);
+  GPB_TRY(P.u_d.ensure((size_t)gmax * P.Kt * sizeof(float)));
+  for (int c0 = 0; c0 < num; c0 += gmax) {
+    const int g = std::min(gmax, num - c0);
+    float* og = out + (int64_t)c0 * nT;
+    lmc_pc_small_kernel<<<g, 256, 2 * (size_t)P.Kt * sizeof(double), st>>>(
+        nullptr, P.C_d.f(), nullptr, P.omega_d.f() + (int64_t)c0 * P.Kt, (const int*)P.rank_d.ptr,
+        (const int*)P.off_d.ptr, P.R, P.T, P.Kt, P.ones_d.f(), P.u_d.f());
+    GPB_CHECK_CUDA(cudaGetLastError());
+    for (int s = 0; s < P.R; ++s)
+      GPB_TRY(k_l_times_u(P.pc[s].L.f(), P.n, P.rank[s], P.u_d.f() + (int64_t)P.off[s] * g,
+                          g * P.T, og, P.n, 1.f, 1.f, og, st));
+  }
+  return GPB_OK;
+}
+
+
 struct LmcOp : LinOp {
   std::vector<gpb_provider*> prov;
   int R = 0, T = 0;
@@ -47,6 +200,8 @@ struct LmcOp : LinOp {
   DBuf A_d, noise_d, tmp;
   Engine E;                     // persistent engine over nT rows
   BBMMState S;                  // persistent CG state (warm starts)
+  Precond pc;                   // rank > 0: the LMC preconditioner below is active
+  LmcPrecond lp;
 
   int upload() {
     GPB_TRY(A_d.ensure(A.size() * sizeof(float)));
@@ -82,12 +237,116 @@ struct LmcOp : LinOp {
   }
 };
 
+
+// Builds P from the current A_s, noise_t and latent kernels (rank_req <= 0 clears it).
+int lmc_build_precond(LmcOp& op, int rank_req) {
+  op.pc.rank = 0;
+  op.pc.lmc = nullptr;
+  op.pc.logdet = 0.0;
+  if (rank_req <= 0) return GPB_OK;
+  LmcPrecond& P = op.lp;
+  const int R = op.R, T = op.T;
+  const int64_t n = op.n;
+  P.R = R;
+  P.T = T;
+  P.n = n;
+  P.pc.assign(R, Precond());
+  P.rank.assign(R, 0);
+  P.off.assign(R, 0);
+  cudaStream_t st = op.E.st;
+  // 1. Per-latent factors L_s of K_s (no noise).
+  for (int s = 0; s < R; ++s) {
+    Engine Es;
+    GPB_TRY(Es.init(op.prov[s], Dist()));
+    Es.st = st;
+    GPB_TRY(precond_build(Es, rank_req, P.pc[s], false));
+    P.rank[s] = P.pc[s].rank;
+  }
+  int Kt = 0;
+  for (int s = 0; s < R; ++s) {
+    P.off[s] = Kt;
+    Kt += T * P.rank[s];
+  }
+  GPB_REQUIRE(Kt <= 3072, GPB_ERR_UNSUPPORTED,
+              "LMC preconditioner: latents x tasks x rank = %d exceeds 3072", Kt);
+  P.Kt = Kt;
+  // 2. C_s = chol(A_s) (1e-4 diagonal jitter if A_s is not positive definite).
+  P.C.assign((size_t)R * T * T, 0.f);
+  for (int s = 0; s < R; ++s) {
+    std::vector<double> A((size_t)T * T), Lo((size_t)T * T);
+    for (int q = 0; q < T * T; ++q) A[q] = op.A[(size_t)s * T * T + q];
+    if (!cholesky_lower(A.data(), T, Lo.data())) {
+      for (int i = 0; i < T; ++i) A[(size_t)i * T + i] += 1e-4;
+      GPB_REQUIRE(cholesky_lower(A.data(), T, Lo.data()), GPB_ERR_NUMERIC,
+                  "LMC preconditioner: A_%d is not positive definite", s);
+    }
+    for (int q = 0; q < T * T; ++q) P.C[(size_t)s * T * T + q] = (float)Lo[q];
+  }
+  P.noise.assign(op.noise.begin(), op.noise.end());
+  for (float v : P.noise)
+    GPB_REQUIRE(v > 0.f, GPB_ERR_INVALID, "LMC preconditioner needs positive task noise");
+  // 3. M = I + sum_{s1,s2} (C_s1^T D^{-1} C_s2) (x) (L_s1^T L_s2).
+  std::vector<double> M((size_t)Kt * Kt, 0.0);
+  for (int q = 0; q < Kt; ++q) M[(size_t)q * Kt + q] = 1.0;
+  for (int s1 = 0; s1 < R; ++s1)
+    for (int s2 = 0; s2 < R; ++s2) {
+      const int r1 = P.rank[s1], r2 = P.rank[s2];
+      GPB_TRY(k_ltv(P.pc[s1].L.f(), n, r1, P.pc[s2].L.f(), n, r2, op.E.red, st));
+      std::vector<double> ltl((size_t)r1 * r2);  // ltl[c * r1 + k] = (L_s1^T L_s2)[k][c]
+      GPB_CHECK_CUDA(cudaMemcpyAsync(ltl.data(), op.E.red.sums.ptr, ltl.size() * sizeof(double),
+                                     cudaMemcpyDeviceToHost, st));
+      GPB_CHECK_CUDA(cudaStreamSynchronize(st));
+      for (int j1 = 0; j1 < T; ++j1)
+        for (int j2 = 0; j2 < T; ++j2) {
+          double g = 0.0;
+          for (int t = 0; t < T; ++t)
+            g += (double)P.C[((size_t)s1 * T + t) * T + j1] * P.C[((size_t)s2 * T + t) * T + j2] /
+                 (double)P.noise[t];
+          if (g == 0.0) continue;
+          for (int k1 = 0; k1 < r1; ++k1)
+            for (int k2 = 0; k2 < r2; ++k2)
+              M[(size_t)(P.off[s1] + j1 * r1 + k1) * Kt + P.off[s2] + j2 * r2 + k2] +=
+                  g * ltl[(size_t)k2 * r1 + k1];
+        }
+    }
+  std::vector<double> Minv((size_t)Kt * Kt);
+  double ldM = 0.0;
+  GPB_REQUIRE(spd_inverse(M.data(), Kt, Minv.data(), &ldM), GPB_ERR_NUMERIC,
+              "LMC preconditioner: I + U^T D^-1 U is not positive definite");
+  P.logdet = ldM;
+  for (int t = 0; t < T; ++t) P.logdet += (double)n * std::log((double)P.noise[t]);
+  // 4. Device copies.
+  std::vector<float> dinv(T), dsqrt(T), ones(T, 1.f);
+  for (int t = 0; t < T; ++t) {
+    dinv[t] = 1.f / P.noise[t];
+    dsqrt[t] = std::sqrt(P.noise[t]);
+  }
+  auto up = [&](DBuf& b, const void* src, size_t bytes) -> int {
+    GPB_TRY(b.ensure(bytes));
+    GPB_CHECK_CUDA(cudaMemcpyAsync(b.ptr, src, bytes, cudaMemcpyHostToDevice, st));
+    return GPB_OK;
+  };
+  GPB_TRY(up(P.C_d, P.C.data(), P.C.size() * sizeof(float)));
+  GPB_TRY(up(P.Minv_d, Minv.data(), Minv.size() * sizeof(double)));
+  GPB_TRY(up(P.dinv_d, dinv.data(), T * sizeof(float)));
+  GPB_TRY(up(P.dsqrt_d, dsqrt.data(), T * sizeof(float)));
+  GPB_TRY(up(P.ones_d, ones.data(), T * sizeof(float)));
+  GPB_TRY(up(P.rank_d, P.rank.data(), R * sizeof(int)));
+  GPB_TRY(up(P.off_d, P.off.data(), R * sizeof(int)));
+  GPB_CHECK_CUDA(cudaStreamSynchronize(st));
+  op.pc.rank = Kt;
+  op.pc.logdet = P.logdet;
+  op.pc.lmc = &P;
+  return GPB_OK;
+}
+
 // Gradients of the LMC NLL (per nT, as the reference normalises):
 //   kernel params of latent s: (-1/2 a^T (A_s (x) dK_s) a + 1/2 mean_k u_k^T (A_s (x) dK_s) w_k) / nT
 //   A_s[i][j]:                 1/2 (-a_i^T K_s a_j + mean_k u_{k,i}^T K_s w_{k,j}) / nT
 //   noise_t:                   1/2 (-a_t^T a_t + mean_k u_{k,t}^T w_{k,t}) / nT
-// with a = alpha, u_k = probe solutions (scaled), w_k = unnormalised probes.
-int lmc_bbmm_gradients(Engine& E, BBMMState& S, float* sol, const float* sampled, int num_probes,
+// with a = alpha, u_k = probe solutions (scaled), w_k = P^{-1} z_k (the unnormalised
+// probes z_k themselves when there is no preconditioner).
+int lmc_bbmm_gradients(Engine& E, BBMMState& S, float* sol, const float* rf, int num_probes,
                        BBMMResult& R) {
   LmcOp* op = static_cast<LmcOp*>(E.op);
   const int T = op->T, Rl = op->R;
@@ -98,7 +357,7 @@ int lmc_bbmm_gradients(Engine& E, BBMMState& S, float* sol, const float* sampled
   GPB_TRY(S.bfull.ensure((size_t)K * nT * sizeof(float)));
   float* Wf = S.bfull.f();
   GPB_TRY(k_copy(Wf, sol, nT, st));
-  GPB_TRY(k_copy(Wf + nT, sampled, (int64_t)num_probes * nT, st));
+  GPB_TRY(k_copy(Wf + nT, rf, (int64_t)num_probes * nT, st));
   DBuf kw, aw;
   GPB_TRY(kw.ensure((size_t)K * nT * sizeof(float)));
   GPB_TRY(aw.ensure((size_t)K * nT * sizeof(float)));
@@ -254,8 +513,8 @@ int gpb_lmc_bbmm(gpb_lmc* h, const float* y_centered_host, int32_t num_probes, i
   GPB_CHECK_CUDA(cudaMemcpyAsync(op.S.yc.ptr, y_centered_host, E.n * sizeof(float),
                                  cudaMemcpyHostToDevice, E.st));
   BBMMResult R;
-  GPB_TRY(bbmm_step(E, nullptr, op.S, num_probes, max_cg_iter, max_tridiag_iter, cg_tol, iteration,
-                    recycle != 0, R));
+  GPB_TRY(bbmm_step(E, op.pc.rank > 0 ? &op.pc : nullptr, op.S, num_probes, max_cg_iter,
+                    max_tridiag_iter, cg_tol, iteration, recycle != 0, R));
   *nll_out = R.nll;
   for (size_t q = 0; q < R.grads.size(); ++q) kernel_grads_out[q] = R.grads[q];
   for (size_t q = 0; q < R.grad_A.size(); ++q) grad_A_out[q] = R.grad_A[q];
@@ -269,6 +528,40 @@ int gpb_lmc_bbmm(gpb_lmc* h, const float* y_centered_host, int32_t num_probes, i
     GPB_CHECK_CUDA(cudaStreamSynchronize(E.st));
   }
   if (cg_iters_out) *cg_iters_out = R.cg_iters;
+  return provider_check_device_error(op.prov[0]);
+}
+
+int gpb_lmc_build_precond(gpb_lmc* h, int32_t rank, int32_t* ranks_out, double* logdet_out) {
+  clear_error();
+  GPB_REQUIRE(h, GPB_ERR_INVALID, "null argument");
+  LmcOp& op = h->op;
+  GPB_CHECK_CUDA(cudaSetDevice(op.prov[0]->device));
+  GPB_TRY(lmc_build_precond(op, rank));
+  if (ranks_out)
+    for (int s = 0; s < op.R; ++s) ranks_out[s] = op.pc.rank > 0 ? op.lp.rank[s] : 0;
+  if (logdet_out) *logdet_out = op.pc.logdet;
+  return provider_check_device_error(op.prov[0]);
+}
+
+int gpb_lmc_precond_apply(gpb_lmc* h, float* out_dev, const float* v_dev, int64_t ncols) {
+  GPB_REQUIRE(h && out_dev && v_dev && ncols >= 0, GPB_ERR_INVALID, "bad arguments");
+  LmcOp& op = h->op;
+  GPB_REQUIRE(op.pc.rank > 0, GPB_ERR_INVALID, "no LMC preconditioner built");
+  GPB_CHECK_CUDA(cudaSetDevice(op.prov[0]->device));
+  if (ncols == 0) return GPB_OK;
+  GPB_TRY(precond_apply(op.E, op.pc, v_dev, out_dev, (int)ncols));
+  GPB_CHECK_CUDA(cudaStreamSynchronize(op.E.st));
+  return provider_check_device_error(op.prov[0]);
+}
+
+int gpb_lmc_precond_sample(gpb_lmc* h, float* out_dev, int32_t num, uint64_t seed) {
+  GPB_REQUIRE(h && out_dev && num >= 0, GPB_ERR_INVALID, "bad arguments");
+  LmcOp& op = h->op;
+  GPB_REQUIRE(op.pc.rank > 0, GPB_ERR_INVALID, "no LMC preconditioner built");
+  GPB_CHECK_CUDA(cudaSetDevice(op.prov[0]->device));
+  if (num == 0) return GPB_OK;
+  GPB_TRY(precond_sample(op.E, op.pc, num, seed, out_dev));
+  GPB_CHECK_CUDA(cudaStreamSynchronize(op.E.st));
   return provider_check_device_error(op.prov[0]);
 }
 

@@ -138,7 +138,7 @@ __global__ void pc_column_kernel(const float* __restrict__ X, int d, int64_t r0,
   if (mask[i] > 0.5f) diag[i] -= col * col;
 }
 
-int precond_build(Engine& E, int rank_req, Precond& P) {
+int precond_build(Engine& E, int rank_req, Precond& P, bool finalize) {
   P.rank = 0;
   P.logdet = 0.0;
   P.noise = E.p->noise;
@@ -190,7 +190,7 @@ int precond_build(Engine& E, int rank_req, Precond& P) {
   GPB_CHECK_CUDA(cudaMemcpyAsync(&act, actual, sizeof(int), cudaMemcpyDeviceToHost, st));
   GPB_CHECK_CUDA(cudaStreamSynchronize(st));
   P.rank = std::max(1, std::min(act, rmax));
-  return precond_finalize(E, P);
+  return finalize ? precond_finalize(E, P) : GPB_OK;
 }
 
 // M = L^T L; Minv = (M + max(noise, 1e-6) I)^{-1} (pivoted_cholesky.mojo:1083-1207);
@@ -226,6 +226,7 @@ int precond_finalize(Engine& E, Precond& P) {
 
 // out = P^{-1} v = (v - L (L^T L + s I)^{-1} L^T v) / sigma^2 (in place allowed).
 int precond_apply(Engine& E, Precond& P, const float* v, float* out, int t) {
+  if (P.lmc) return lmc_precond_apply(E, *P.lmc, v, out, t);
   const int r = P.rank;
   GPB_TRY(k_ltv(P.L.f(), E.nl, r, v, E.nl, t, E.red, E.st));
   GPB_TRY(E.allreduce_sum(E.red.sums.d(), (size_t)t * r));
@@ -239,6 +240,7 @@ int precond_apply(Engine& E, Precond& P, const float* v, float* out, int t) {
 // N(0, P) probes: L z_rank + sqrt(noise) z_noise with hash Gaussians seeded
 // `seed` ([num][rank] layout) and seed + 1e6 ([num][n] layout).
 int precond_sample(Engine& E, Precond& P, int num, uint64_t seed, float* out) {
+  if (P.lmc) return lmc_precond_sample(E, *P.lmc, num, seed, out);
   const int r = P.rank;
   GPB_TRY(P.u.ensure((size_t)num * r * sizeof(float)));
   GPB_TRY(k_gaussian(P.u.f(), 1, (int64_t)num * r, (int64_t)num * r, (int64_t)num * r, 0, seed, E.st));

@@ -264,13 +264,15 @@ int bbmm_step(Engine& E, Precond* P, BBMMState& S, int num_probes, int max_cg, i
   // 6. Gradients: a = [alpha | u_j * |z_j|], b = [alpha | P^{-1} z_j].
   float* A = sol;  // probe columns scaled by probe norms in place
   GPB_TRY(k_scale_cols(A + nl, nl, nl, num_probes, pnorms_dev, 0, st));
-  if (E.op) return lmc_bbmm_gradients(E, S, A, sampled, num_probes, R);
   float* B = S.rf.f();
   GPB_TRY(k_copy(B, sol, nl, st));
   if (use_p)
     GPB_TRY(precond_apply(E, *P, sampled, B + nl, num_probes));
   else
     GPB_TRY(k_copy(B + nl, sampled, (int64_t)num_probes * nl, st));
+  // LMC: the right factors are P^{-1} z (z when unpreconditioned), as in the
+  // single-output path.
+  if (E.op) return lmc_bbmm_gradients(E, S, A, B + nl, num_probes, R);
   const int P_ = p->dk.nparams;
   std::vector<double> data(P_, 0.0), trace(P_, 0.0);
   {

@@ -38,7 +38,7 @@ int k_sub_scalar(float* v, int64_t count, float s, cudaStream_t st);
 int alpha_cg(Engine& E, const float* y_local, float* x, int max_iter, float tol, int* iters_out);
 // LMC gradients from the BBMM solution (lmc.cu); sol holds [alpha | scaled
 // probe solutions], sampled the unnormalised probes.
-int lmc_bbmm_gradients(Engine& E, BBMMState& S, float* sol, const float* sampled, int num_probes,
+int lmc_bbmm_gradients(Engine& E, BBMMState& S, float* sol, const float* rf, int num_probes,
                        BBMMResult& R);
 
 }  // namespace gpb

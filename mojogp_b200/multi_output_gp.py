@@ -5,8 +5,13 @@ for the matrix-free route and its training loop train_lmc_jit
 (mojogp/kernels/jit/jit_lmc.mojo:699-1529): per-latent kernels K_s sharing X,
 coregionalisation A_s = L_s L_s^T + diag(v_s) with softplus diagonals, per-task
 noise and per-task constant means, Adam with gradient clip 10, NLL per n*T.
-The LMC preconditioner (lmc_preconditioner.mojo) is not built: training runs
-unpreconditioned mBCG.
+mBCG is preconditioned by the sum-of-Kronecker Woodbury preconditioner
+(lmc_preconditioner.mojo), rebuilt when a kernel parameter or a task noise has
+moved by more than `precond_rebuild_threshold` relative to the last build
+(jit_lmc.mojo:1047-1100). Predictive variances follow predict_lmc
+(kernels/jit/jit_engine_lmc_bindings.mojo:1102-1395): per-latent LOVE
+variances with the mean task noise, weighted by the squared row norms of A_s,
+plus the task noise.
 """
 from __future__ import annotations
 
@@ -75,6 +80,31 @@ class LMC:
         return {"nll": nll.value, "kgrads": kg, "gA": gA, "gnoise": gn, "sum_alpha": sa,
                 "alpha": alpha, "cg_iters": it.value}
 
+    def build_precond(self, rank: int):
+        """Build (rank > 0) or remove (rank <= 0) the LMC preconditioner from the
+        current A_s, noise and latent kernels; returns (per-latent ranks, log|P|)."""
+        ranks = np.zeros(self.R, np.int32)
+        ld = C.c_double()
+        _lib.call("gpb_lmc_build_precond", C.c_void_p(self.handle), int(rank),
+                  ranks.ctypes.data_as(C.POINTER(C.c_int32)), C.byref(ld))
+        return ranks, ld.value
+
+    def precond_apply_host(self, V: np.ndarray) -> np.ndarray:
+        """P^{-1} V for task-blocked columns V [ncols, T*n] (host arrays)."""
+        from .provider import DeviceBuffer
+        V = np.ascontiguousarray(V, np.float32).reshape(-1, self.T * self.n)
+        vd = DeviceBuffer.from_host(V, self.providers[0].device)
+        od = DeviceBuffer(V.shape, self.providers[0].device)
+        _lib.call("gpb_lmc_precond_apply", C.c_void_p(self.handle), od.cptr, vd.cptr, V.shape[0])
+        return od.download()
+
+    def precond_sample_host(self, num: int, seed: int) -> np.ndarray:
+        from .provider import DeviceBuffer
+        od = DeviceBuffer((num, self.T * self.n), self.providers[0].device)
+        _lib.call("gpb_lmc_precond_sample", C.c_void_p(self.handle), od.cptr, int(num),
+                  C.c_uint64(seed))
+        return od.download()
+
     def solve(self, rhs: np.ndarray, max_cg: int = 300, tol: float = 1e-3):
         r = np.ascontiguousarray(rhs, np.float32).ravel()
         x = np.zeros_like(r)
@@ -100,7 +130,8 @@ class MultiOutputLMCGP:
 
     def __init__(self, kernels: list, num_probes: int = 10, max_cg_iterations: int = 200,
                  cg_tolerance: float = 1.0, max_tridiag_iterations: int = 30, ard: bool = False,
-                 init_mean=None, device: int = 0):
+                 init_mean=None, device: int = 0, preconditioner_rank: int = 15,
+                 precond_rebuild_threshold: float = 0.5, lanczos_rank: int = 0):
         ks = []
         for k in kernels:
             if isinstance(k, str):
@@ -121,6 +152,9 @@ class MultiOutputLMCGP:
         self.ard = ard
         self.init_mean = init_mean
         self.device = device
+        self.precond_rank = int(preconditioner_rank)
+        self.precond_rebuild_threshold = float(precond_rebuild_threshold)
+        self.lanczos_rank = int(lanczos_rank)
         self._lmc: Optional[LMC] = None
 
     def _state_to_A(self, L, raw_L_diag, raw_var):
@@ -177,7 +211,11 @@ class MultiOutputLMCGP:
         Yb = Y.T.astype(np.float64)  # [T, n] task-blocked
         best = None
         hist = []
+        cg_hist = []
         t_step = 0
+        last_build = None  # (kernel params, noise) at the last preconditioner build
+        self.precond_rebuild_count = 0
+        self.precond_ranks = None
 
         def adam(idx, g):
             m[idx] = 0.9 * m[idx] + 0.1 * g
@@ -193,11 +231,24 @@ class MultiOutputLMCGP:
             A, Lf = self._state_to_A(L, raw_L_diag, raw_var)
             noise = np.array([_sp(r) for r in raw_noise])
             self._lmc.set_coregion(A, noise)
+            if self.precond_rank > 0:
+                cur = (np.concatenate([[_sp(r) for r in rp] for rp in raw_p]), noise.copy())
+                rebuild = last_build is None
+                if not rebuild:
+                    rel = [np.max(np.abs(c - l) / (np.abs(l) + 1e-8)) if c.size else 0.0
+                           for c, l in zip(cur, last_build)]
+                    rebuild = max(rel) > self.precond_rebuild_threshold
+                if rebuild:
+                    if last_build is not None:
+                        self.precond_rebuild_count += 1
+                    self.precond_ranks, _ = self._lmc.build_precond(self.precond_rank)
+                    last_build = cur
             yc = (Yb - raw_mean[:, None]).astype(np.float32)
             res = self._lmc.bbmm(yc, self.num_probes, self.max_cg_iter, self.max_tridiag_iter,
                                  self.cg_tol, it, it > 0)
             nll = res["nll"]
             hist.append(nll)
+            cg_hist.append(res["cg_iters"])
             if not np.isfinite(nll):
                 if best is None:
                     raise FloatingPointError("LMC NLL is not finite at the initial parameters")
@@ -248,6 +299,7 @@ class MultiOutputLMCGP:
         self.A, self.noise, self.mean_ = A, noise, raw_mean
         self.params_ = [np.array([_sp(r) for r in rp]) for rp in raw_p]
         self.nll_history = np.array(hist)
+        self.cg_iterations_history = cg_hist
         self.final_nll = best[0]
         yc = (Yb - raw_mean[:, None]).astype(np.float32)
         self._alpha, _ = self._lmc.solve(yc, 300, 1e-3)
@@ -256,11 +308,10 @@ class MultiOutputLMCGP:
     def log_marginal_likelihood(self) -> float:
         return -float(self.final_nll)
 
-    def predict(self, X_test, return_var: bool = False):
+    def predict(self, X_test, return_var: bool = False, return_std: bool = False):
+        """Mean [m, T]; with return_var / return_std also the LOVE variance / std [m, T]."""
         if self._lmc is None:
             raise RuntimeError("model must be fit first")
-        if return_var:
-            raise NotImplementedError("LMC predictive variance is not built in this round")
         Xt = np.ascontiguousarray(X_test, np.float32)
         if Xt.ndim == 1:
             Xt = Xt[:, None]
@@ -270,4 +321,30 @@ class MultiOutputLMCGP:
         for s, prov in enumerate(self._lmc.providers):
             Cs = prov.cross_matvec_host(Xt, alpha)  # [n*, T] = K_s(X*, X) alpha_j
             mean += Cs @ self.A[s].T
-        return (mean + self.mean_[None, :]).astype(np.float32)
+        mean = (mean + self.mean_[None, :]).astype(np.float32)
+        if not (return_var or return_std):
+            return mean
+        from .gp import _DEFAULT_PREDICT_LANCZOS_RANK
+        from .prediction import PredictionCache
+        avg_noise = float(np.mean(self.noise))
+        var = np.zeros((Xt.shape[0], T))
+        for s, prov in enumerate(self._lmc.providers):
+            rank = self.lanczos_rank
+            if rank <= 0:
+                ard = self.kernels_resolved[s].has_ard()
+                rank = max(_DEFAULT_PREDICT_LANCZOS_RANK, 200 if ard else 0)
+            rank = min(rank, n)
+            prov.update_noise(avg_noise)
+            try:
+                cache = PredictionCache(prov, np.zeros(n, np.float32), 0.0, rank)
+                _, v_s = cache.predict(Xt, return_var=True)
+                cache.destroy()
+            finally:
+                prov.update_noise(0.0)
+            latent = np.maximum(v_s.astype(np.float64) - avg_noise, 1e-10)
+            row_w = (self.A[s] ** 2).sum(axis=1)  # sum_t' A_s[t][t']^2
+            var += latent[:, None] * row_w[None, :]
+        var = (var + self.noise[None, :]).astype(np.float32)
+        if return_std:
+            return mean, np.sqrt(var)
+        return mean, var

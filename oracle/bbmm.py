@@ -54,11 +54,15 @@ def gaussian_block(n: int, t: int, seed: int) -> np.ndarray:
 class Precond:
     """Greedy pivoted Cholesky P = L L^T + noise I (precond_method = 0)."""
 
-    def __init__(self, K: np.ndarray, noise: float, rank: int):
+    def __init__(self, K: np.ndarray, noise: float, rank: int, dtype=np.float64):
+        """`dtype` = np.float32 repeats the factorisation in the reference's float32
+        arithmetic (pivoted_cholesky.mojo is FP32); its trailing columns, where the
+        residual diagonal is tiny, carry mostly rounding and shift log|P| visibly."""
         n = K.shape[0]
-        diag = np.diag(K).astype(np.float64).copy()
+        K = np.asarray(K, dtype)
+        diag = np.diag(K).astype(dtype).copy()
         mask = np.ones(n, dtype=bool)
-        L = np.zeros((n, rank))
+        L = np.zeros((n, rank), dtype)
         pivots = []
         actual = rank
         for m in range(rank):
@@ -70,11 +74,11 @@ class Precond:
                 break
             mask[piv] = False
             col = K[:, piv] - L[:, :m] @ L[piv, :m]
-            col = col / math.sqrt(max(maxv, 1e-10))
+            col = col / dtype(math.sqrt(max(maxv, 1e-10)))
             L[:, m] = col
             diag[mask] -= col[mask] ** 2
             pivots.append(piv)
-        self.L = L[:, :actual]
+        self.L = L[:, :actual].astype(np.float64)
         self.rank = actual
         self.pivots = pivots
         self.noise = float(noise)

@@ -4,6 +4,13 @@
              (kernels/jit/jit_lmc.mojo:275-330, lmc_provider.mojo:113-192)
   gradients  kernel params through A_s (x) dK_s; A_s and per-task noise
              (jit_lmc.mojo:582-691); NLL / SLQ as combined_inv_quad_logdet.mojo:452
+  precond    sum-of-Kronecker Woodbury P = sum_s A_s (x) L_s L_s^T + D
+             (lmc_preconditioner.mojo:143-470, built as jit_lmc.mojo:848-900);
+             probes use the library's counter-hash Gaussians (omega seed s,
+             eps seed s + 1e6) instead of the reference's host generator, so
+             preconditioned runs are pinned to this restatement, not to the
+             reference's random stream.
+Test infrastructure only (tests, smoke checks, CPU baseline).
 """
 from __future__ import annotations
 
@@ -28,8 +35,48 @@ def full_operator(specs, params_list, X, A, noise):
     return K, Ks, Gs
 
 
+class LmcPrecond:
+    """P = sum_s (C_s (x) L_s)(C_s (x) L_s)^T + D; Woodbury apply, log|P|, N(0, P) probes."""
+
+    def __init__(self, Ks, A, noise, rank, factor_dtype=np.float64):
+        A = np.asarray(A, np.float64)
+        self.R, self.T = A.shape[0], A.shape[1]
+        self.n = Ks[0].shape[0]
+        self.noise = np.asarray(noise, np.float64)
+        # greedy pivoted Cholesky of each K_s
+        self.L = [ob.Precond(K, 1.0, rank, factor_dtype).L for K in Ks]
+        self.C = []
+        for s in range(self.R):
+            try:
+                self.C.append(np.linalg.cholesky(A[s]))
+            except np.linalg.LinAlgError:
+                self.C.append(np.linalg.cholesky(A[s] + 1e-4 * np.eye(self.T)))
+        # U = [C_s (x) L_s] with column order (s, j, k) -> off_s + j r_s + k
+        self.U = np.concatenate([np.kron(self.C[s], self.L[s]) for s in range(self.R)], axis=1)
+        self.d = np.repeat(self.noise, self.n)
+        M = np.eye(self.U.shape[1]) + self.U.T @ (self.U / self.d[:, None])
+        self.Minv = np.linalg.inv(M)
+        _, ldM = np.linalg.slogdet(M)
+        self.logdet = self.n * float(np.sum(np.log(self.noise))) + ldM
+        self.ranks = [L.shape[1] for L in self.L]
+
+    def dense(self):
+        return self.U @ self.U.T + np.diag(self.d)
+
+    def apply(self, V):
+        w = V / self.d[:, None]
+        return w - (self.U @ (self.Minv @ (self.U.T @ w))) / self.d[:, None]
+
+    def sample(self, num, seed):
+        nT = self.n * self.T
+        Kt = self.U.shape[1]
+        eps = ob.gaussian_block(nT, num, seed + 1000000)
+        om = ob.hash_gaussian(np.arange(num * Kt, dtype=np.uint64), seed).reshape(num, Kt).T
+        return np.sqrt(self.d)[:, None] * eps + self.U @ om
+
+
 def lmc_bbmm(specs, params_list, X, Y_centered, A, noise, num_probes, max_cg, max_tridiag, tol,
-             iteration=0):
+             iteration=0, precond_rank=0):
     """Y_centered [n, T]. Returns nll, kernel grads (concatenated), grad_A, grad_noise."""
     X = np.asarray(X, np.float64)
     n = X.shape[0]
@@ -39,16 +86,18 @@ def lmc_bbmm(specs, params_list, X, Y_centered, A, noise, num_probes, max_cg, ma
     y = np.asarray(Y_centered, np.float64).T.reshape(nT)  # task-blocked
     K, Ks, Gs = full_operator(specs, params_list, X, A, np.asarray(noise, np.float64))
     seed = iteration * 104729 + 42
-    W = ob.gaussian_block(nT, num_probes, seed)
-    pn = np.linalg.norm(W, axis=0)
-    rhs = np.concatenate([y[:, None], W / pn], axis=1)
+    P = LmcPrecond(Ks, A, noise, precond_rank) if precond_rank > 0 else None
+    Z = P.sample(num_probes, seed) if P is not None else ob.gaussian_block(nT, num_probes, seed)
+    pn = np.linalg.norm(Z, axis=0)
+    rhs = np.concatenate([y[:, None], Z / pn], axis=1)
     rn = np.linalg.norm(rhs, axis=0)
-    x, iters, dg, od = ob.mbcg(K, rhs / rn, max_cg, max_tridiag, tol)
+    x, iters, dg, od = ob.mbcg(K, rhs / rn, max_cg, max_tridiag, tol, P)
+    W = P.apply(Z) if P is not None else Z  # right factors
     sol = x * rn
     alpha = sol[:, 0]
     U = sol[:, 1:] * pn
     inv_quad = float(y @ alpha)
-    logdet = ob.slq_logdet(dg[1:], od[1:], nT)
+    logdet = ob.slq_logdet(dg[1:], od[1:], nT) + (P.logdet if P is not None else 0.0)
     PI = float(np.float32(3.14159265358979323846))
     nll = (0.5 * inv_quad + 0.5 * logdet + 0.5 * nT * math.log(2 * PI)) / nT
     kgrads = []

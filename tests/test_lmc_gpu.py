@@ -73,3 +73,78 @@ def test_lmc_fit_predict_config4_small(gpb_lib):
     mean = gp.predict(X[:500])
     r2 = 1 - np.mean((mean - Y[:500]) ** 2) / np.var(Y[:500])
     assert mean.shape == (500, 4) and r2 > 0.8
+
+
+def _ill_conditioned(n=150, d=2, T=3, seed=5):
+    """Small task noise: the regime the LMC preconditioner exists for."""
+    X, ks, ps, A, noise, provs, lmc = _setup(n, d, T, seed)
+    noise = np.array([0.01, 0.02, 0.015][:T], np.float32)
+    lmc.set_coregion(A, noise)
+    return X, ks, ps, A, noise, provs, lmc
+
+
+def test_lmc_precond_apply_logdet_sample_vs_oracle(gpb_lib):
+    X, ks, ps, A, noise, provs, lmc = _ill_conditioned()
+    n, T = X.shape[0], A.shape[1]
+    ranks, logdet = lmc.build_precond(10)
+    Ks = [olmc.ok.kernel_matrix(k.to_spec(2), p, X.astype(np.float64)) for k, p in zip(ks, ps)]
+    # The greedy factor is float32 on the device as in the reference; at task
+    # noise 0.01 its rounding-level trailing columns move log|P| by ~4 against a
+    # float64 factor, so log|P| is pinned to the float32 factorisation.
+    P = olmc.LmcPrecond(Ks, A, noise, 10, factor_dtype=np.float32)
+    assert list(ranks) == P.ranks
+    assert abs(logdet - P.logdet) < 1e-5 * abs(P.logdet)
+    V = np.random.default_rng(3).standard_normal((6, T * n)).astype(np.float32)
+    got = lmc.precond_apply_host(V)
+    ref = P.apply(V.T.astype(np.float64)).T
+    assert np.linalg.norm(got - ref) / np.linalg.norm(ref) < 1e-4
+    Z = lmc.precond_sample_host(5, 77)
+    Zr = P.sample(5, 77).T
+    assert np.linalg.norm(Z - Zr) / np.linalg.norm(Zr) < 1e-4
+    # rank <= 0 removes it
+    r0, ld0 = lmc.build_precond(0)
+    assert ld0 == 0.0 and not r0.any()
+
+
+def test_lmc_bbmm_preconditioned_vs_oracle(gpb_lib):
+    X, ks, ps, A, noise, provs, lmc = _ill_conditioned()
+    rng = np.random.default_rng(4)
+    Y = rng.standard_normal((X.shape[0], A.shape[1])).astype(np.float32)
+    yc = (Y - Y.mean(0)).T.copy()
+    plain = lmc.bbmm(yc, 8, 200, 30, 1e-2, 1, False)
+    lmc.build_precond(15)
+    got = lmc.bbmm(yc, 8, 200, 30, 1e-2, 1, False)
+    ref = olmc.lmc_bbmm([k.to_spec(2) for k in ks], ps, X, Y - Y.mean(0), A, noise, 8, 200, 30,
+                        1e-2, iteration=1, precond_rank=15)
+    # The preconditioner cuts the iteration count of the same solve.
+    assert got["cg_iters"] < plain["cg_iters"]
+    assert abs(got["cg_iters"] - ref["cg_iters"]) <= 10
+    assert abs(got["nll"] - ref["nll"]) < 1e-3 * abs(ref["nll"])
+    np.testing.assert_allclose(got["gnoise"], ref["gnoise"], rtol=0,
+                               atol=1e-2 * np.abs(ref["gnoise"]).max())
+    np.testing.assert_allclose(got["gA"], ref["gA"], rtol=0, atol=1e-2 * np.abs(ref["gA"]).max())
+
+
+def test_lmc_predict_variance_vs_exact_latents(gpb_lib):
+    X, Y = synthetic.config4(n=600)
+    gp = MultiOutputLMCGP(kernels=[RBF(), Matern32()], num_probes=8)
+    gp.fit(X, Y, max_iterations=5, learning_rate=0.05)
+    gp.lanczos_rank = 600  # LOVE rank = n: the root is exact up to float32
+    Xt = X[:50]
+    mean, var = gp.predict(Xt, return_var=True)
+    _, std = gp.predict(Xt, return_std=True)
+    np.testing.assert_allclose(std, np.sqrt(var), rtol=1e-6)
+    # predict_lmc's formula with exact latent posteriors:
+    avg = float(np.mean(gp.noise))
+    Xd = X.astype(np.float64)
+    ref = np.zeros_like(var, dtype=np.float64)
+    for s, (k, p) in enumerate(zip(gp.kernels_resolved, gp.params_)):
+        spec = k.to_spec(X.shape[1])
+        K = olmc.ok.kernel_matrix(spec, p, Xd)
+        Ks = olmc.ok.kernel_matrix(spec, p, Xd[:50], Xd)
+        kss = np.diag(olmc.ok.kernel_matrix(spec, p, Xd[:50]))
+        lat = kss - np.einsum("ij,ji->i", Ks, np.linalg.solve(K + avg * np.eye(len(X)), Ks.T))
+        ref += np.maximum(lat, 1e-10)[:, None] * (gp.A[s] ** 2).sum(axis=1)[None, :]
+    ref += gp.noise[None, :]
+    assert var.shape == (50, 4)
+    np.testing.assert_allclose(var, ref, rtol=2e-3, atol=1e-4)
