@@ -297,6 +297,13 @@ int gpb_prediction_cache_destroy(gpb_prediction_cache* c);
 typedef struct gpb_lmc gpb_lmc;
 int gpb_lmc_create(gpb_provider* const* providers, int32_t num_latents, int32_t num_tasks,
                    gpb_lmc** out);
+/* Row-sharded LMC (no reference counterpart): rank g owns data rows
+ * [n g / W, n (g+1) / W) of every task, so device-side column blocks
+ * (gpb_lmc_matvec, gpb_lmc_precond_apply / _sample) are this rank's
+ * [ncols][T][n_local]; host-side y / alpha / rhs stay full [T][n] on every
+ * rank. comm NULL = one GPU (same as gpb_lmc_create). */
+int gpb_lmc_create_sharded(gpb_provider* const* providers, int32_t num_latents, int32_t num_tasks,
+                           gpb_comm* comm, gpb_lmc** out);
 int gpb_lmc_destroy(gpb_lmc* h);
 /* A [R][T][T] (symmetric PSD coregionalisation matrices), noise [T]. */
 int gpb_lmc_set_coregion(gpb_lmc* h, const float* A, const float* noise);

@@ -75,6 +75,7 @@ SIGNATURES = {
     "gpb_forward_matvec_noalloc": [P, P, P, c_i64],
     "gpb_tc_selftest": [c_i32, c_i32, P, P, P],
     "gpb_lmc_create": [P, c_i32, c_i32, PP],
+    "gpb_lmc_create_sharded": [P, c_i32, c_i32, P, PP],
     "gpb_lmc_destroy": [P],
     "gpb_lmc_set_coregion": [P, P, P],
     "gpb_lmc_matvec": [P, P, P, c_i64],

@@ -105,8 +105,8 @@ int Engine::coldots(int npairs, const float* const* a, const float* const* b, in
 int Engine::matvec(float* v_local, int64_t v_ld, int t, float* out, int64_t out_ld,
                    const float* update_z, const float* update_beta) {
   if (op) {
-    GPB_REQUIRE(dist.world == 1 && v_ld == nl && out_ld == nl, GPB_ERR_UNSUPPORTED,
-                "operator matvec needs a single GPU and dense column blocks");
+    GPB_REQUIRE(v_ld == nl && out_ld == nl, GPB_ERR_UNSUPPORTED,
+                "operator matvec needs dense column blocks");
     if (update_beta) GPB_TRY(k_update_p(v_local, update_z, update_beta, nl, v_ld, t, st));
     return op->apply(v_local, v_ld, t, out, st);
   }

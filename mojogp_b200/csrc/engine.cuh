@@ -51,8 +51,11 @@ struct Reducer {
 // Kronecker products); when set, Engine::matvec delegates to it.
 struct LinOp {
   virtual ~LinOp() = default;
-  // out = A v for [t][ld] blocks over all rows (single GPU).
+  // out = A v for [t][ld] blocks over this rank's rows.
   virtual int apply(const float* v, int64_t ld, int t, float* out, cudaStream_t st) = 0;
+  // t probe columns ~ N(0, I) over this rank's rows, indexed so that every
+  // sharding draws the same numbers.
+  virtual int gaussian(float* out, int t, uint64_t seed, cudaStream_t st) = 0;
 };
 
 struct Engine {
@@ -84,6 +87,8 @@ struct Engine {
 
 // Kernel launchers (engine_kernels.cu).
 int k_fill(float* p, int64_t count, float v, cudaStream_t st);
+int k_gaussian_tasks(float* out, int cols, int T, int64_t nl, int64_t n, int64_t r0, uint64_t seed,
+                     cudaStream_t st);
 int k_copy(float* dst, const float* src, int64_t count, cudaStream_t st);
 int k_gaussian(float* out, int t, int64_t nl, int64_t ld, int64_t n_global, int64_t row0,
                uint64_t seed, cudaStream_t st);

@@ -81,6 +81,30 @@ int k_gaussian(float* out, int t, int64_t nl, int64_t ld, int64_t n_global, int6
   return GPB_OK;
 }
 
+// Task-blocked probes over this rank's data rows: element (c, t, i) of a local
+// [cols][T][nl] block takes the global index c*T*n + t*n + r0 + i, so every
+// sharding draws the same numbers as one GPU.
+__global__ void gaussian_tasks_kernel(float* out, int cols, int T, int64_t nl, int64_t n,
+                                      int64_t r0, uint64_t seed) {
+  const int64_t idx = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int64_t per_col = (int64_t)T * nl;
+  if (idx >= (int64_t)cols * per_col) return;
+  const int64_t c = idx / per_col;
+  const int64_t rem = idx - c * per_col;
+  const int64_t t = rem / nl;
+  const int64_t i = rem - t * nl;
+  out[idx] = hash_gaussian((uint64_t)((c * T + t) * n + r0 + i), seed);
+}
+int k_gaussian_tasks(float* out, int cols, int T, int64_t nl, int64_t n, int64_t r0, uint64_t seed,
+                     cudaStream_t st) {
+  const int64_t total = (int64_t)cols * T * nl;
+  if (total <= 0) return GPB_OK;
+  gaussian_tasks_kernel<<<(unsigned)ceil_div(total, 256), 256, 0, st>>>(out, cols, T, nl, n, r0,
+                                                                       seed);
+  GPB_CHECK_CUDA(cudaGetLastError());
+  return GPB_OK;
+}
+
 // v[c][i] *= scale[c] (or /= scale[c] when inverse).
 __global__ void scale_cols_kernel(float* v, int64_t ld, int64_t nl, int t, const float* scale,
                                   int inverse) {

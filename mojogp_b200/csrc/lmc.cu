@@ -18,7 +18,11 @@
 #include "numerics.h"
 #include "train.cuh"
 
+struct gpb_comm;  // defined in train.cu
+
 namespace gpb {
+
+int engine_from_comm(gpb_provider* p, gpb_comm* c, Engine& E);
 
 // out[c][t][i] (+)= sum_j A[t][j] kv[c][j][i]  (+ noise[t] v[c][t][i] when v != null)
 __global__ void lmc_mix_kernel(float* __restrict__ out, const float* __restrict__ kv,
@@ -115,7 +119,8 @@ __global__ void lmc_task_scale_kernel(float* __restrict__ out, const float* __re
 
 struct LmcPrecond {
   int R = 0, T = 0, Kt = 0;
-  int64_t n = 0;
+  int64_t n = 0;            // data rows (global)
+  int64_t nl = 0, r0 = 0;   // this rank's data rows [r0, r0 + nl)
   std::vector<int> rank, off;       // per latent
   std::vector<Precond> pc;          // per latent: L_s
   std::vector<float> C;             // [R][T][T] row-major lower Cholesky of A_s
@@ -133,12 +138,12 @@ struct LmcPrecond {
 };
 
 int lmc_precond_apply(Engine& E, LmcPrecond& P, const float* v, float* out, int t) {
-  const int64_t nT = (int64_t)P.T * P.n, cnt = (int64_t)t * nT;
+  const int64_t nT = (int64_t)P.T * P.nl, cnt = (int64_t)t * nT;
   cudaStream_t st = E.st;
-  GPB_TRY(P.w_d.ensure((size_t)cnt * sizeof(float)));
+  GPB_TRY(P.w_d.ensure((size_t)std::max<int64_t>(cnt, 1) * sizeof(float)));
   float* w = P.w_d.f();
-  lmc_task_scale_kernel<<<(unsigned)ceil_div(cnt, 256), 256, 0, st>>>(w, v, P.dinv_d.f(), P.T, P.n,
-                                                                     cnt);
+  lmc_task_scale_kernel<<<(unsigned)ceil_div(std::max<int64_t>(cnt, 1), 256), 256, 0, st>>>(
+      w, v, P.dinv_d.f(), P.T, std::max<int64_t>(P.nl, 1), cnt);
   GPB_CHECK_CUDA(cudaGetLastError());
   const int gmax = P.group_cols(t);
   GPB_TRY(P.Z_d.ensure((size_t)gmax * P.Kt * sizeof(double)));
@@ -148,7 +153,8 @@ int lmc_precond_apply(Engine& E, LmcPrecond& P, const float* v, float* out, int 
     const float* wg = w + (int64_t)c0 * nT;
     float* og = out + (int64_t)c0 * nT;
     for (int s = 0; s < P.R; ++s) {
-      GPB_TRY(k_ltv(P.pc[s].L.f(), P.n, P.rank[s], wg, P.n, g * P.T, E.red, st));
+      GPB_TRY(k_ltv(P.pc[s].L.f(), P.nl, P.rank[s], wg, P.nl, g * P.T, E.red, st));
+      GPB_TRY(E.allreduce_sum(E.red.sums.d(), (size_t)g * P.T * P.rank[s]));
       GPB_CHECK_CUDA(cudaMemcpyAsync(P.Z_d.d() + (int64_t)P.off[s] * g, E.red.sums.ptr,
                                      (size_t)g * P.T * P.rank[s] * sizeof(double),
                                      cudaMemcpyDeviceToDevice, st));
@@ -158,19 +164,22 @@ int lmc_precond_apply(Engine& E, LmcPrecond& P, const float* v, float* out, int 
         (const int*)P.off_d.ptr, P.R, P.T, P.Kt, P.dinv_d.f(), P.u_d.f());
     GPB_CHECK_CUDA(cudaGetLastError());
     for (int s = 0; s < P.R; ++s)
-      GPB_TRY(k_l_times_u(P.pc[s].L.f(), P.n, P.rank[s], P.u_d.f() + (int64_t)P.off[s] * g,
-                          g * P.T, s == 0 ? wg : og, P.n, 1.f, -1.f, og, st));
+      GPB_TRY(k_l_times_u(P.pc[s].L.f(), P.nl, P.rank[s], P.u_d.f() + (int64_t)P.off[s] * g,
+                          g * P.T, s == 0 ? wg : og, P.nl, 1.f, -1.f, og, st));
   }
   E.p->launches += 1 + (int64_t)((t + gmax - 1) / gmax) * (2 * P.R + 1);
   return GPB_OK;
 }
 
 int lmc_precond_sample(Engine& E, LmcPrecond& P, int num, uint64_t seed, float* out) {
-  const int64_t nT = (int64_t)P.T * P.n, cnt = (int64_t)num * nT;
+  const int64_t nT = (int64_t)P.T * P.nl, cnt = (int64_t)num * nT;
   cudaStream_t st = E.st;
-  GPB_TRY(k_gaussian(out, num, nT, nT, nT, 0, seed + 1000000ull, st));
-  lmc_task_scale_kernel<<<(unsigned)ceil_div(cnt, 256), 256, 0, st>>>(out, out, P.dsqrt_d.f(), P.T,
-                                                                     P.n, cnt);
+  GPB_TRY(k_gaussian_tasks(out, num, P.T, P.nl, P.n, P.r0, seed + 1000000ull, st));
+  if (cnt > 0) {
+    lmc_task_scale_kernel<<<(unsigned)ceil_div(cnt, 256), 256, 0, st>>>(out, out, P.dsqrt_d.f(),
+                                                                       P.T, P.nl, cnt);
+    GPB_CHECK_CUDA(cudaGetLastError());
+  }
   GPB_CHECK_CUDA(cudaGetLastError());
   GPB_TRY(P.omega_d.ensure((size_t)num * P.Kt * sizeof(float)));
   const int64_t no = (int64_t)num * P.Kt;
@@ -185,8 +194,8 @@ int lmc_precond_sample(Engine& E, LmcPrecond& P, int num, uint64_t seed, float* 
         (const int*)P.off_d.ptr, P.R, P.T, P.Kt, P.ones_d.f(), P.u_d.f());
     GPB_CHECK_CUDA(cudaGetLastError());
     for (int s = 0; s < P.R; ++s)
-      GPB_TRY(k_l_times_u(P.pc[s].L.f(), P.n, P.rank[s], P.u_d.f() + (int64_t)P.off[s] * g,
-                          g * P.T, og, P.n, 1.f, 1.f, og, st));
+      GPB_TRY(k_l_times_u(P.pc[s].L.f(), P.nl, P.rank[s], P.u_d.f() + (int64_t)P.off[s] * g,
+                          g * P.T, og, P.nl, 1.f, 1.f, og, st));
   }
   return GPB_OK;
 }
@@ -195,10 +204,12 @@ int lmc_precond_sample(Engine& E, LmcPrecond& P, int num, uint64_t seed, float* 
 struct LmcOp : LinOp {
   std::vector<gpb_provider*> prov;
   int R = 0, T = 0;
-  int64_t n = 0;
+  int64_t n = 0;                // data rows (global)
+  int64_t nl = 0, r0 = 0;       // this rank's data rows [r0, r0 + nl); all tasks of a row
   std::vector<float> A, noise;  // host copies
-  DBuf A_d, noise_d, tmp;
-  Engine E;                     // persistent engine over nT rows
+  DBuf A_d, noise_d, tmp, vfull;
+  Engine Ed;                    // data-row engine (row split, all-gather of columns)
+  Engine E;                     // operator engine over the local [T][nl] task blocks
   BBMMState S;                  // persistent CG state (warm starts)
   Precond pc;                   // rank > 0: the LMC preconditioner below is active
   LmcPrecond lp;
@@ -213,29 +224,74 @@ struct LmcOp : LinOp {
     return GPB_OK;
   }
 
-  // kv_s = K_s v for `cols` task-blocked columns (no noise), v [cols][T][n].
-  int latent_kv(int s, const float* v, int cols, float* out, cudaStream_t st) {
+  // Full task-blocked columns [cols][T][n] from local blocks [cols][T][nl].
+  int gather(const float* v_local, int cols, const float** full) {
+    if (Ed.dist.world == 1) {
+      *full = v_local;
+      return GPB_OK;
+    }
+    GPB_TRY(vfull.ensure((size_t)cols * T * n * sizeof(float)));
+    GPB_TRY(Ed.allgather_cols(v_local, nl, cols * T, vfull.f()));
+    *full = vfull.f();
+    return GPB_OK;
+  }
+
+  // out_local [cols][T][nl] = K_s(X_local, X) v_full (no noise), v_full [cols][T][n].
+  int latent_kv_full(int s, const float* v_full, int cols, float* out, cudaStream_t st) {
     gpb_provider* p = prov[s];
     if (p->xs_dirty) {
       GPB_TRY(provider_refresh_xs(p));
       GPB_CHECK_CUDA(cudaStreamSynchronize(p->stream));
     }
-    return provider_kv(p, p->Xs_d, n, v, n, (int64_t)cols * T, out, n, false, 0, st);
+    return provider_kv(p, p->Xs_d + r0 * p->DP, nl, v_full, n, (int64_t)cols * T, out, nl, false,
+                       0, st);
+  }
+
+  // Same from local blocks.
+  int latent_kv(int s, const float* v_local, int cols, float* out, cudaStream_t st) {
+    const float* vf = nullptr;
+    GPB_TRY(gather(v_local, cols, &vf));
+    return latent_kv_full(s, vf, cols, out, st);
   }
 
   int apply(const float* v, int64_t ld, int t, float* out, cudaStream_t st) override {
-    const int64_t total = (int64_t)t * T * n;
+    const int64_t total = (int64_t)t * T * nl;
+    if (total == 0) return GPB_OK;
     GPB_TRY(tmp.ensure((size_t)total * sizeof(float)));
+    const float* vf = nullptr;
+    GPB_TRY(gather(v, t, &vf));
     for (int s = 0; s < R; ++s) {
-      GPB_TRY(latent_kv(s, v, t, tmp.f(), st));
+      GPB_TRY(latent_kv_full(s, vf, t, tmp.f(), st));
       lmc_mix_kernel<<<(unsigned)ceil_div(total, 256), 256, 0, st>>>(
-          out, tmp.f(), A_d.f() + (size_t)s * T * T, T, n, t, s > 0 ? 1 : 0, noise_d.f(),
+          out, tmp.f(), A_d.f() + (size_t)s * T * T, T, nl, t, s > 0 ? 1 : 0, noise_d.f(),
           s == R - 1 ? v : nullptr);
       GPB_CHECK_CUDA(cudaGetLastError());
     }
     return GPB_OK;
   }
+
+  // Host [T][n] -> this rank's local block [T][nl].
+  int to_local(const float* host, float* local) {
+    for (int t = 0; t < T && nl > 0; ++t)
+      GPB_CHECK_CUDA(cudaMemcpyAsync(local + (int64_t)t * nl, host + (int64_t)t * n + r0,
+                                     nl * sizeof(float), cudaMemcpyHostToDevice, E.st));
+    return GPB_OK;
+  }
+  // Local block [T][nl] -> host [T][n] (gathered over the ranks).
+  int to_host(const float* local, float* host) {
+    const float* full = nullptr;
+    GPB_TRY(gather(local, 1, &full));
+    GPB_CHECK_CUDA(cudaMemcpyAsync(host, full, (size_t)T * n * sizeof(float), cudaMemcpyDeviceToHost,
+                                   E.st));
+    GPB_CHECK_CUDA(cudaStreamSynchronize(E.st));
+    return GPB_OK;
+  }
+
+  int gaussian(float* out, int t, uint64_t seed, cudaStream_t st) override {
+    return k_gaussian_tasks(out, t, T, nl, n, r0, seed, st);
+  }
 };
+
 
 
 // Builds P from the current A_s, noise_t and latent kernels (rank_req <= 0 clears it).
@@ -250,6 +306,8 @@ int lmc_build_precond(LmcOp& op, int rank_req) {
   P.R = R;
   P.T = T;
   P.n = n;
+  P.nl = op.nl;
+  P.r0 = op.r0;
   P.pc.assign(R, Precond());
   P.rank.assign(R, 0);
   P.off.assign(R, 0);
@@ -257,7 +315,7 @@ int lmc_build_precond(LmcOp& op, int rank_req) {
   // 1. Per-latent factors L_s of K_s (no noise).
   for (int s = 0; s < R; ++s) {
     Engine Es;
-    GPB_TRY(Es.init(op.prov[s], Dist()));
+    GPB_TRY(Es.init(op.prov[s], op.Ed.dist));
     Es.st = st;
     GPB_TRY(precond_build(Es, rank_req, P.pc[s], false));
     P.rank[s] = P.pc[s].rank;
@@ -291,7 +349,8 @@ int lmc_build_precond(LmcOp& op, int rank_req) {
   for (int s1 = 0; s1 < R; ++s1)
     for (int s2 = 0; s2 < R; ++s2) {
       const int r1 = P.rank[s1], r2 = P.rank[s2];
-      GPB_TRY(k_ltv(P.pc[s1].L.f(), n, r1, P.pc[s2].L.f(), n, r2, op.E.red, st));
+      GPB_TRY(k_ltv(P.pc[s1].L.f(), P.nl, r1, P.pc[s2].L.f(), P.nl, r2, op.E.red, st));
+      GPB_TRY(op.E.allreduce_sum(op.E.red.sums.d(), (size_t)r1 * r2));
       std::vector<double> ltl((size_t)r1 * r2);  // ltl[c * r1 + k] = (L_s1^T L_s2)[k][c]
       GPB_CHECK_CUDA(cudaMemcpyAsync(ltl.data(), op.E.red.sums.ptr, ltl.size() * sizeof(double),
                                      cudaMemcpyDeviceToHost, st));
@@ -350,49 +409,74 @@ int lmc_bbmm_gradients(Engine& E, BBMMState& S, float* sol, const float* rf, int
                        BBMMResult& R) {
   LmcOp* op = static_cast<LmcOp*>(E.op);
   const int T = op->T, Rl = op->R;
-  const int64_t n = op->n, nT = (int64_t)T * n;
+  const int64_t nl = op->nl, nTl = (int64_t)T * nl;  // local rows of every task
   const int K = 1 + num_probes;  // column blocks: 0 = alpha, k >= 1 = probes
   cudaStream_t st = E.st;
-  // Wf = [alpha | w_1 .. w_np] (task-blocked columns of length nT)
-  GPB_TRY(S.bfull.ensure((size_t)K * nT * sizeof(float)));
+  // Local dots over this rank's rows, summed over the ranks, to the host.
+  auto dots = [&](const float* a, const float* b, int64_t ld, int cols, std::vector<double>& h) {
+    const float* pa[1] = {a};
+    const float* pb[1] = {b};
+    GPB_TRY(k_coldots(1, pa, pb, ld, nl, cols, E.red, st));
+    GPB_TRY(E.allreduce_sum(E.red.sums.d(), (size_t)cols));
+    h.resize(cols);
+    GPB_CHECK_CUDA(cudaMemcpyAsync(h.data(), E.red.sums.ptr, cols * sizeof(double),
+                                   cudaMemcpyDeviceToHost, st));
+    GPB_CHECK_CUDA(cudaStreamSynchronize(st));
+    return GPB_OK;
+  };
+  // Wf = [alpha | w_1 .. w_np] (local task-blocked columns of length T * nl)
+  GPB_TRY(S.bfull.ensure((size_t)std::max<int64_t>(K * nTl, 1) * sizeof(float)));
   float* Wf = S.bfull.f();
-  GPB_TRY(k_copy(Wf, sol, nT, st));
-  GPB_TRY(k_copy(Wf + nT, rf, (int64_t)num_probes * nT, st));
-  DBuf kw, aw;
-  GPB_TRY(kw.ensure((size_t)K * nT * sizeof(float)));
-  GPB_TRY(aw.ensure((size_t)K * nT * sizeof(float)));
-  const double dnT = (double)nT;
+  GPB_TRY(k_copy(Wf, sol, nTl, st));
+  GPB_TRY(k_copy(Wf + nTl, rf, (int64_t)num_probes * nTl, st));
+  DBuf kw, aw, awfull;
+  GPB_TRY(kw.ensure((size_t)std::max<int64_t>(K * nTl, 1) * sizeof(float)));
+  GPB_TRY(aw.ensure((size_t)std::max<int64_t>(K * nTl, 1) * sizeof(float)));
+  const double dnT = (double)T * op->n;
   R.grad_A.assign((size_t)Rl * T * T, 0.0);
-  std::vector<double> kgrads;
+  std::vector<double> kgrads, h;
   for (int s = 0; s < Rl; ++s) {
     gpb_provider* p = op->prov[s];
     // A_s gradients from K_s Wf.
     GPB_TRY(op->latent_kv(s, Wf, K, kw.f(), st));
     for (int i = 0; i < T; ++i)
       for (int j = 0; j < T; ++j) {
-        const float* a[1] = {sol + (int64_t)i * n};
-        const float* b[1] = {kw.f() + (int64_t)j * n};
-        // K columns with stride nT: column k = block k of task i / j
-        GPB_TRY(k_coldots(1, a, b, nT, n, K, E.red, st));
-        std::vector<double> h(K);
-        GPB_CHECK_CUDA(cudaMemcpyAsync(h.data(), E.red.sums.ptr, K * sizeof(double),
-                                       cudaMemcpyDeviceToHost, st));
-        GPB_CHECK_CUDA(cudaStreamSynchronize(st));
+        // K columns with stride T * nl: column k = block k of task i / j
+        GPB_TRY(dots(sol + (int64_t)i * nl, kw.f() + (int64_t)j * nl, nTl, K, h));
         double tr = 0.0;
         for (int k = 1; k < K; ++k) tr += h[k];
         R.grad_A[((size_t)s * T + i) * T + j] = 0.5 * (-h[0] + tr / num_probes) / dnT;
       }
-    // Kernel-parameter gradients: b = (A_s (x) I) Wf.
-    const int64_t total = (int64_t)K * nT;
-    lmc_mix_kernel<<<(unsigned)ceil_div(total, 256), 256, 0, st>>>(
-        aw.f(), Wf, op->A_d.f() + (size_t)s * T * T, T, n, K, 0, nullptr, nullptr);
-    GPB_CHECK_CUDA(cudaGetLastError());
+    // Kernel-parameter gradients: b = (A_s (x) I) Wf over all rows.
+    const int64_t total = (int64_t)K * nTl;
+    if (total > 0) {
+      lmc_mix_kernel<<<(unsigned)ceil_div(total, 256), 256, 0, st>>>(
+          aw.f(), Wf, op->A_d.f() + (size_t)s * T * T, T, nl, K, 0, nullptr, nullptr);
+      GPB_CHECK_CUDA(cudaGetLastError());
+    }
+    const float* awf = aw.f();
+    if (op->Ed.dist.world > 1) {
+      GPB_TRY(awfull.ensure((size_t)K * T * op->n * sizeof(float)));
+      GPB_TRY(op->Ed.allgather_cols(aw.f(), nl, K * T, awfull.f()));
+      awf = awfull.f();
+    }
     const int P = p->dk.nparams;
-    std::vector<double> data(P), trace(P);
-    GPB_TRY(provider_bilinear_rows_nd(p, sol, n, aw.f(), (int64_t)K * T, 0, n, T, data.data(),
-                                      trace.data(), st));
+    std::vector<double> both(2 * P, 0.0);
+    if (nl > 0)
+      GPB_TRY(provider_bilinear_rows_nd(p, sol, nl, awf, (int64_t)K * T, op->r0, op->r0 + nl, T,
+                                        both.data(), both.data() + P, st));
+    if (op->Ed.dist.world > 1) {
+      DBuf gb;
+      GPB_TRY(gb.ensure(both.size() * sizeof(double)));
+      GPB_CHECK_CUDA(cudaMemcpyAsync(gb.ptr, both.data(), both.size() * sizeof(double),
+                                     cudaMemcpyHostToDevice, st));
+      GPB_TRY(E.allreduce_sum(gb.d(), both.size()));
+      GPB_CHECK_CUDA(cudaMemcpyAsync(both.data(), gb.ptr, both.size() * sizeof(double),
+                                     cudaMemcpyDeviceToHost, st));
+      GPB_CHECK_CUDA(cudaStreamSynchronize(st));
+    }
     for (int q = 0; q < P; ++q) {
-      double g = (-0.5 * data[q] + 0.5 * trace[q] / num_probes) / dnT;
+      double g = (-0.5 * both[q] + 0.5 * both[P + q] / num_probes) / dnT;
       if (!std::isfinite(g)) g = 0.0;
       kgrads.push_back(g);
     }
@@ -401,23 +485,12 @@ int lmc_bbmm_gradients(Engine& E, BBMMState& S, float* sol, const float* rf, int
   R.grad_noise_task.assign(T, 0.0);
   R.sum_alpha_task.assign(T, 0.0);
   for (int t = 0; t < T; ++t) {
-    const float* a[2] = {sol + (int64_t)t * n, sol + (int64_t)t * n};
-    const float* b[2] = {Wf + (int64_t)t * n, S.ones.f()};
-    GPB_TRY(k_coldots(1, a, b, nT, n, K, E.red, st));
-    std::vector<double> h(K);
-    GPB_CHECK_CUDA(cudaMemcpyAsync(h.data(), E.red.sums.ptr, K * sizeof(double),
-                                   cudaMemcpyDeviceToHost, st));
-    GPB_CHECK_CUDA(cudaStreamSynchronize(st));
+    GPB_TRY(dots(sol + (int64_t)t * nl, Wf + (int64_t)t * nl, nTl, K, h));
     double tr = 0.0;
     for (int k = 1; k < K; ++k) tr += h[k];
     R.grad_noise_task[t] = 0.5 * (-h[0] + tr / num_probes) / dnT;
-    const float* a1[1] = {sol + (int64_t)t * n};
-    const float* b1[1] = {S.ones.f()};
-    GPB_TRY(k_coldots(1, a1, b1, n, n, 1, E.red, st));
-    double sa = 0.0;
-    GPB_CHECK_CUDA(cudaMemcpyAsync(&sa, E.red.sums.ptr, sizeof(double), cudaMemcpyDeviceToHost, st));
-    GPB_CHECK_CUDA(cudaStreamSynchronize(st));
-    R.sum_alpha_task[t] = sa;
+    GPB_TRY(dots(sol + (int64_t)t * nl, S.ones.f(), nl, 1, h));
+    R.sum_alpha_task[t] = h[0];
   }
   R.grads = kgrads;
   return GPB_OK;
@@ -433,8 +506,8 @@ struct gpb_lmc {
 
 extern "C" {
 
-int gpb_lmc_create(gpb_provider* const* providers, int32_t num_latents, int32_t num_tasks,
-                   gpb_lmc** out) {
+int gpb_lmc_create_sharded(gpb_provider* const* providers, int32_t num_latents,
+                           int32_t num_tasks, gpb_comm* comm, gpb_lmc** out) {
   clear_error();
   GPB_REQUIRE(providers && out && num_latents >= 1 && num_tasks >= 1, GPB_ERR_INVALID,
               "bad LMC arguments");
@@ -446,28 +519,42 @@ int gpb_lmc_create(gpb_provider* const* providers, int32_t num_latents, int32_t 
   GPB_CHECK_CUDA(cudaSetDevice(providers[0]->device));
   gpb_lmc* h = new gpb_lmc();
   LmcOp& op = h->op;
+  int s = engine_from_comm(providers[0], comm, op.Ed);
+  if (s != GPB_OK) {
+    delete h;
+    return s;
+  }
   op.prov.assign(providers, providers + num_latents);
   op.R = num_latents;
   op.T = num_tasks;
   op.n = n;
+  op.nl = op.Ed.nl;
+  op.r0 = op.Ed.r0;
   op.A.assign((size_t)num_latents * num_tasks * num_tasks, 0.f);
-  for (int s = 0; s < num_latents; ++s)
-    for (int t = 0; t < num_tasks; ++t) op.A[((size_t)s * num_tasks + t) * num_tasks + t] = 1.f;
+  for (int q = 0; q < num_latents; ++q)
+    for (int t = 0; t < num_tasks; ++t) op.A[((size_t)q * num_tasks + t) * num_tasks + t] = 1.f;
   op.noise.assign(num_tasks, 0.1f);
   op.E.p = providers[0];
   op.E.op = &op;
   op.E.st = providers[0]->stream;
-  op.E.n = op.E.nl = n * num_tasks;
-  op.E.r0 = 0;
-  op.E.r1 = op.E.n;
-  op.E.nl_pad = op.E.n;
-  int s = op.upload();
+  op.E.dist = op.Ed.dist;
+  op.E.n = n * num_tasks;
+  op.E.nl = op.nl * num_tasks;
+  op.E.r0 = op.r0 * num_tasks;
+  op.E.r1 = op.E.r0 + op.E.nl;
+  op.E.nl_pad = std::max<int64_t>(op.E.nl, 1);
+  s = op.upload();
   if (s != GPB_OK) {
     delete h;
     return s;
   }
   *out = h;
   return GPB_OK;
+}
+
+int gpb_lmc_create(gpb_provider* const* providers, int32_t num_latents, int32_t num_tasks,
+                   gpb_lmc** out) {
+  return gpb_lmc_create_sharded(providers, num_latents, num_tasks, nullptr, out);
 }
 
 int gpb_lmc_destroy(gpb_lmc* h) {
@@ -510,8 +597,7 @@ int gpb_lmc_bbmm(gpb_lmc* h, const float* y_centered_host, int32_t num_probes, i
   GPB_CHECK_CUDA(cudaSetDevice(op.prov[0]->device));
   Engine& E = op.E;
   GPB_TRY(op.S.ensure(E, 1 + num_probes, max_tridiag_iter));
-  GPB_CHECK_CUDA(cudaMemcpyAsync(op.S.yc.ptr, y_centered_host, E.n * sizeof(float),
-                                 cudaMemcpyHostToDevice, E.st));
+  GPB_TRY(op.to_local(y_centered_host, op.S.yc.f()));
   BBMMResult R;
   GPB_TRY(bbmm_step(E, op.pc.rank > 0 ? &op.pc : nullptr, op.S, num_probes, max_cg_iter,
                     max_tridiag_iter, cg_tol, iteration, recycle != 0, R));
@@ -522,11 +608,7 @@ int gpb_lmc_bbmm(gpb_lmc* h, const float* y_centered_host, int32_t num_probes, i
     grad_noise_out[t] = R.grad_noise_task[t];
     sum_alpha_out[t] = R.sum_alpha_task[t];
   }
-  if (alpha_out) {
-    GPB_CHECK_CUDA(cudaMemcpyAsync(alpha_out, op.S.sol.ptr, E.n * sizeof(float),
-                                   cudaMemcpyDeviceToHost, E.st));
-    GPB_CHECK_CUDA(cudaStreamSynchronize(E.st));
-  }
+  if (alpha_out) GPB_TRY(op.to_host(op.S.sol.f(), alpha_out));
   if (cg_iters_out) *cg_iters_out = R.cg_iters;
   return provider_check_device_error(op.prov[0]);
 }
@@ -572,13 +654,12 @@ int gpb_lmc_solve(gpb_lmc* h, const float* rhs_host, int32_t max_cg_iter, float 
   GPB_CHECK_CUDA(cudaSetDevice(op.prov[0]->device));
   Engine& E = op.E;
   DBuf y, x;
-  GPB_TRY(y.ensure((size_t)E.n * sizeof(float)));
-  GPB_TRY(x.ensure((size_t)E.n * sizeof(float)));
-  GPB_CHECK_CUDA(cudaMemcpyAsync(y.ptr, rhs_host, E.n * sizeof(float), cudaMemcpyHostToDevice, E.st));
+  GPB_TRY(y.ensure((size_t)std::max<int64_t>(E.nl, 1) * sizeof(float)));
+  GPB_TRY(x.ensure((size_t)std::max<int64_t>(E.nl, 1) * sizeof(float)));
+  GPB_TRY(op.to_local(rhs_host, y.f()));
   int it = 0;
   GPB_TRY(alpha_cg(E, y.f(), x.f(), max_cg_iter, cg_tol, &it));
-  GPB_CHECK_CUDA(cudaMemcpyAsync(x_host_out, x.ptr, E.n * sizeof(float), cudaMemcpyDeviceToHost, E.st));
-  GPB_CHECK_CUDA(cudaStreamSynchronize(E.st));
+  GPB_TRY(op.to_host(x.f(), x_host_out));
   if (iters_out) *iters_out = it;
   return provider_check_device_error(op.prov[0]);
 }

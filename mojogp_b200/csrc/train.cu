@@ -216,6 +216,8 @@ int bbmm_step(Engine& E, Precond* P, BBMMState& S, int num_probes, int max_cg, i
   float* sampled = S.sampled.f();
   if (use_p)
     GPB_TRY(precond_sample(E, *P, num_probes, seed, sampled));
+  else if (E.op)
+    GPB_TRY(E.op->gaussian(sampled, num_probes, seed, st));
   else
     GPB_TRY(k_gaussian(sampled, num_probes, nl, nl, E.n, E.r0, seed, st));
   float* probes = S.probes.f();
@@ -578,12 +580,19 @@ int gpb_comm_destroy(gpb_comm* c) {
 }
 
 static int comm_host_reduce(gpb_comm* c, double* vals, int64_t count, ncclRedOp_t op) {
-  GPB_REQUIRE(c && vals && count >= 0 && count <= 4096, GPB_ERR_INVALID, "bad reduce arguments");
+  GPB_REQUIRE(c && (vals || count == 0) && count >= 0, GPB_ERR_INVALID, "bad reduce arguments");
   GPB_CHECK_CUDA(cudaSetDevice(c->device));
-  GPB_CHECK_CUDA(cudaMemcpyAsync(c->buf, vals, count * sizeof(double), cudaMemcpyHostToDevice, c->st));
-  ncclResult_t r = ncclAllReduce(c->buf, c->buf, count, ncclDouble, op, c->dist.comm, c->st);
-  GPB_REQUIRE(r == ncclSuccess, GPB_ERR_NCCL, "ncclAllReduce: %s", ncclGetErrorString(r));
-  GPB_CHECK_CUDA(cudaMemcpyAsync(vals, c->buf, count * sizeof(double), cudaMemcpyDeviceToHost, c->st));
+  // The communicator's staging buffer holds 4096 doubles: larger arrays go
+  // through it in pieces.
+  for (int64_t off = 0; off < count; off += 4096) {
+    const int64_t m = std::min<int64_t>(4096, count - off);
+    GPB_CHECK_CUDA(cudaMemcpyAsync(c->buf, vals + off, m * sizeof(double), cudaMemcpyHostToDevice,
+                                   c->st));
+    ncclResult_t r = ncclAllReduce(c->buf, c->buf, m, ncclDouble, op, c->dist.comm, c->st);
+    GPB_REQUIRE(r == ncclSuccess, GPB_ERR_NCCL, "ncclAllReduce: %s", ncclGetErrorString(r));
+    GPB_CHECK_CUDA(cudaMemcpyAsync(vals + off, c->buf, m * sizeof(double), cudaMemcpyDeviceToHost,
+                                   c->st));
+  }
   GPB_CHECK_CUDA(cudaStreamSynchronize(c->st));
   return GPB_OK;
 }

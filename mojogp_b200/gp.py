@@ -275,7 +275,10 @@ class SingleOutputGP:
         cache = self.prepare_prediction_cache("love" if want_var else "mean_only",
                                               max_root_decomposition_size, max_cg_iterations,
                                               cg_tolerance)
-        mean, var = cache.predict(Xt, return_var=want_var)
+        if self._comm is not None and self._comm.world > 1:
+            mean, var = cache.predict_sharded(Xt, self._comm, return_var=want_var)
+        else:
+            mean, var = cache.predict(Xt, return_var=want_var)
         if var is None:
             var = np.zeros_like(mean)
         std = np.sqrt(np.maximum(var, 0))

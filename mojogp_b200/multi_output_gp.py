@@ -45,14 +45,23 @@ def _dsp(x):
 class LMC:
     """Thin owner of a gpb_lmc handle over R providers."""
 
-    def __init__(self, providers: List[Provider], num_tasks: int):
+    def __init__(self, providers: List[Provider], num_tasks: int, comm=None):
+        """comm: a distributed.Communicator to shard the data rows over the ranks
+        (all tasks of a row on one GPU); host-side arrays stay full on every rank."""
         self.providers = providers
         self.T = num_tasks
         self.R = len(providers)
         self.n = providers[0].n
+        self.comm = comm
+        if comm is not None and comm.world > 1:
+            from .distributed import shard_bounds
+            self.r0, self.r1 = shard_bounds(self.n, comm.world, comm.rank)
+        else:
+            self.r0, self.r1 = 0, self.n
         arr = (C.c_void_p * self.R)(*[p.handle for p in providers])
         h = C.c_void_p()
-        _lib.call("gpb_lmc_create", C.cast(arr, C.c_void_p), self.R, num_tasks, C.byref(h))
+        _lib.call("gpb_lmc_create_sharded", C.cast(arr, C.c_void_p), self.R, num_tasks,
+                  C.c_void_p(comm.handle) if comm is not None else None, C.byref(h))
         self.handle = h.value
 
     def set_coregion(self, A: np.ndarray, noise: np.ndarray) -> None:
@@ -90,9 +99,9 @@ class LMC:
         return ranks, ld.value
 
     def precond_apply_host(self, V: np.ndarray) -> np.ndarray:
-        """P^{-1} V for task-blocked columns V [ncols, T*n] (host arrays)."""
+        """P^{-1} V for task-blocked columns V [ncols, T*n_local] (this rank's rows)."""
         from .provider import DeviceBuffer
-        V = np.ascontiguousarray(V, np.float32).reshape(-1, self.T * self.n)
+        V = np.ascontiguousarray(V, np.float32).reshape(-1, self.T * (self.r1 - self.r0))
         vd = DeviceBuffer.from_host(V, self.providers[0].device)
         od = DeviceBuffer(V.shape, self.providers[0].device)
         _lib.call("gpb_lmc_precond_apply", C.c_void_p(self.handle), od.cptr, vd.cptr, V.shape[0])
@@ -100,7 +109,7 @@ class LMC:
 
     def precond_sample_host(self, num: int, seed: int) -> np.ndarray:
         from .provider import DeviceBuffer
-        od = DeviceBuffer((num, self.T * self.n), self.providers[0].device)
+        od = DeviceBuffer((num, self.T * (self.r1 - self.r0)), self.providers[0].device)
         _lib.call("gpb_lmc_precond_sample", C.c_void_p(self.handle), od.cptr, int(num),
                   C.c_uint64(seed))
         return od.download()
@@ -168,7 +177,8 @@ class MultiOutputLMCGP:
         return A, L
 
     def fit(self, X, Y, max_iterations: int = 100, learning_rate: float = 0.05,
-            initial_noise: float = 0.1, method: str = "matrix_free", verbose: bool = False):
+            initial_noise: float = 0.1, method: str = "matrix_free", verbose: bool = False,
+            comm=None):
         if method not in ("matrix_free", "auto"):
             raise NotImplementedError(f"method={method!r}: this build implements matrix-free LMC")
         X = np.ascontiguousarray(X, np.float32)
@@ -188,7 +198,7 @@ class MultiOutputLMCGP:
         masks = [k.engine_trainable_mask() for k in self.kernels_resolved]
         provs = [Provider(X, k, p, 0.0, device=self.device)
                  for k, p in zip(self.kernels_resolved, params0)]
-        self._lmc = LMC(provs, T)
+        self._lmc = LMC(provs, T, comm=comm)
         raw_p = [np.array([_isp(float(v)) for v in p]) for p in params0]
         raw_noise = np.array([_isp(initial_noise)] * T)
         if self.init_mean is None:

@@ -65,6 +65,28 @@ class PredictionCache:
                   _p(var) if var is not None else None)
         return mean, var
 
+    def predict_sharded(self, X_test: np.ndarray, comm, return_var: bool = True):
+        """Each rank predicts its slice of the test rows (rows [m r / W, m (r+1) / W))
+        with the replicated alpha / LOVE root; one all-reduce assembles the full
+        outputs on every rank (X* sharding: no collective on the data path)."""
+        Xt = np.ascontiguousarray(X_test, dtype=np.float32)
+        if Xt.ndim == 1:
+            Xt = Xt[:, None]
+        m = Xt.shape[0]
+        from .distributed import shard_bounds
+        a, b = shard_bounds(m, comm.world, comm.rank)
+        mean_l, var_l = self.predict(Xt[a:b], return_var=return_var) if b > a else \
+            (np.zeros(0, np.float32), np.zeros(0, np.float32) if return_var else None)
+        want_var = return_var and self.rank > 0
+        buf = np.zeros(2 * m if want_var else m)
+        buf[a:b] = mean_l
+        if want_var:
+            buf[m + a:m + b] = var_l
+        buf = comm.allreduce_sum(buf)
+        mean = buf[:m].astype(np.float32)
+        var = buf[m:].astype(np.float32) if want_var else None
+        return mean, var
+
     def destroy(self) -> None:
         if getattr(self, "handle", None):
             _lib.lib().gpb_prediction_cache_destroy(C.c_void_p(self.handle))

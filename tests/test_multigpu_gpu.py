@@ -51,3 +51,19 @@ def test_two_gpu_sharded_engine_matches_one_gpu(gpb_lib, tmp_path):
     np.testing.assert_allclose(two["alpha_head"], one["alpha_head"], rtol=1e-3, atol=1e-4)
     np.testing.assert_allclose(two["mean"], one["mean"], rtol=1e-4, atol=1e-4)
     np.testing.assert_allclose(two["var"], one["var"], rtol=1e-3, atol=1e-5)
+    np.testing.assert_allclose(two["mean_sharded"], one["mean"], rtol=1e-4, atol=1e-4)
+    np.testing.assert_allclose(two["var_sharded"], one["var"], rtol=1e-3, atol=1e-5)
+    np.testing.assert_allclose(one["mean_sharded"], one["mean"], rtol=0, atol=0)
+    bad = []
+    for tag in ("lmc", "lmc_pc"):
+        a, b = one[tag], two[tag]
+        if a["cg"] != b["cg"]:
+            bad.append(f"{tag} cg {a['cg']} vs {b['cg']}")
+        if abs(a["nll"] - b["nll"]) >= 1e-4 * abs(a["nll"]):
+            bad.append(f"{tag} nll {a['nll']} vs {b['nll']}")
+        for key in ("gA", "gnoise", "kgrads", "alpha"):
+            ref, got = np.asarray(a[key]), np.asarray(b[key])
+            err = np.abs(got - ref).max() / max(np.abs(ref).max(), 1e-30)
+            if err >= 1e-3:
+                bad.append(f"{tag} {key} rel err {err:.2e}")
+    assert not bad, "; ".join(bad)
