@@ -287,6 +287,17 @@ int gpb_prediction_cache_root(gpb_prediction_cache* c, float* root_host_out);
 int gpb_predict_with_cache(gpb_prediction_cache* c, const float* xtest_host, int64_t n_test,
                            float* mean_out, float* var_out);
 int gpb_prediction_cache_destroy(gpb_prediction_cache* c);
+/* Replaces predict_variance_exact_jit (jit_prediction.mojo:1352-1788) with the
+ * noise add of predict_from_alpha (2048-2051): per block of block_cols (<= 0:
+ * min(n_test, 512)) test points, K(X, X*) is filled, (K + noise I) V = K(X, X*)
+ * is solved by batched CG (pivoted-Cholesky preconditioner of rank
+ * precond_rank when > 0, relative stop cg_tol), and
+ * var = max(k(x*, x*) - K(x*, X) v, 1e-10) + noise. Training rows are sharded
+ * over comm (NULL = one GPU); every rank returns all n_test variances. */
+int gpb_predict_exact_variance(gpb_provider* p, gpb_comm* comm, const float* xtest_host,
+                               int64_t n_test, int32_t block_cols, int32_t max_cg_iter,
+                               float cg_tol, int32_t precond_rank, float* var_out,
+                               int32_t* cg_iters_out);
 
 /* ------------------------------------------------------------------ LMC
  * Linear model of coregionalisation over R latent providers (same X, n, device):

@@ -74,6 +74,7 @@ SIGNATURES = {
     "gpb_prediction_cache_destroy": [P],
     "gpb_forward_matvec_noalloc": [P, P, P, c_i64],
     "gpb_tc_selftest": [c_i32, c_i32, P, P, P],
+    "gpb_predict_exact_variance": [P, P, P, c_i64, c_i32, c_i32, c_f32, c_i32, P, PI32],
     "gpb_lmc_create": [P, c_i32, c_i32, PP],
     "gpb_lmc_create_sharded": [P, c_i32, c_i32, P, PP],
     "gpb_lmc_destroy": [P],

@@ -5,6 +5,7 @@
 //   compute_lanczos_inv_root_jit            974-1177 (Lanczos + reorth + T^-1/2)
 //   predict_variance_love_from_inv_root_jit 1236-1344, kernel_love_variance 211-232
 //   predict_from_alpha_jit noise add        2048-2051
+//   predict_variance_exact_jit              1352-1788, kernel_exact_variance 235-256
 // B200 changes: every vector update, dot product and the Lanczos
 // re-orthogonalisation (two classical Gram-Schmidt passes as GEMVs over the
 // device-resident basis) run on the GPU, rows sharded across ranks; only
@@ -15,6 +16,8 @@
 
 #include "engine.cuh"
 #include "numerics.h"
+#include "precond.cuh"
+#include "train.cuh"
 
 struct gpb_comm;  // defined in train.cu
 namespace gpb {
@@ -233,6 +236,24 @@ __global__ void love_finish_kernel(const float* __restrict__ V0, const float* __
 
 using namespace gpb;
 
+namespace gpb {
+// out[c][i] = k(x_{r0 + i}, x*_c) over this rank's training rows (raw inputs,
+// tree evaluator), one row of the exact-variance right-hand side per test point.
+__global__ void cross_fill_kernel(const float* __restrict__ X, int64_t r0, int64_t nl, int d,
+                                  const float* __restrict__ Xt, const __grid_constant__ DevKernel K,
+                                  float* __restrict__ out) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int c = blockIdx.y;
+  if (i >= nl) return;
+  float xi[GPB_MAX_DIM], xc[GPB_MAX_DIM];
+  for (int k = 0; k < d; ++k) {
+    xi[k] = X[(r0 + i) * d + k];
+    xc[k] = Xt[(int64_t)c * d + k];
+  }
+  out[(int64_t)c * nl + i] = tree_eval<false>(K, xi, xc, nullptr);
+}
+}  // namespace gpb
+
 extern "C" {
 
 int gpb_compute_alpha(gpb_provider* p, gpb_comm* comm, const float* y_centered_host, int64_t n,
@@ -363,6 +384,69 @@ int gpb_prediction_cache_destroy(gpb_prediction_cache* c) {
   cudaSetDevice(c->p->device);
   delete c;
   return GPB_OK;
+}
+
+int gpb_predict_exact_variance(gpb_provider* p, gpb_comm* comm, const float* xtest_host,
+                               int64_t n_test, int32_t block_cols, int32_t max_cg_iter,
+                               float cg_tol, int32_t precond_rank, float* var_out,
+                               int32_t* cg_iters_out) {
+  clear_error();
+  GPB_REQUIRE(p && xtest_host && var_out && n_test >= 0 && max_cg_iter >= 1, GPB_ERR_INVALID,
+              "bad arguments");
+  if (n_test == 0) return GPB_OK;
+  GPB_CHECK_CUDA(cudaSetDevice(p->device));
+  Engine E;
+  GPB_TRY(engine_from_comm(p, comm, E));
+  cudaStream_t st = E.st;
+  // Block width: all test points up to 512 columns (choose_exact_prediction_block_cols).
+  const int b = (int)std::min<int64_t>(n_test, block_cols > 0 ? block_cols : 512);
+  Precond P;
+  if (precond_rank > 0) GPB_TRY(precond_build(E, precond_rank, P));
+  BBMMState S;
+  GPB_TRY(S.ensure(E, b, 1));
+  DBuf xt, cross, diag;
+  GPB_TRY(xt.ensure((size_t)n_test * p->d * sizeof(float)));
+  GPB_TRY(cross.ensure((size_t)b * std::max<int64_t>(E.nl, 1) * sizeof(float)));
+  GPB_TRY(diag.ensure((size_t)b * sizeof(float)));
+  GPB_CHECK_CUDA(cudaMemcpyAsync(xt.ptr, xtest_host, (size_t)n_test * p->d * sizeof(float),
+                                 cudaMemcpyHostToDevice, st));
+  std::vector<float> norms, dg(b);
+  int total_iters = 0;
+  for (int64_t c0 = 0; c0 < n_test; c0 += b) {
+    const int m = (int)std::min<int64_t>(b, n_test - c0);
+    const float* xb = xt.f() + c0 * p->d;
+    // 1. K(X_local, X*_block) [m][nl] and k(x*, x*).
+    if (E.nl > 0) {
+      dim3 grid((unsigned)ceil_div(E.nl, 128), (unsigned)m);
+      cross_fill_kernel<<<grid, 128, 0, st>>>(p->X_d, E.r0, E.nl, p->d, xb, p->dk, cross.f());
+      GPB_CHECK_CUDA(cudaGetLastError());
+    }
+    GPB_TRY(gpb_extract_diagonal_test(p, diag.f(), xb, m));
+    // 2. (K + noise I) V = K(X, X*) by batched CG on normalised columns.
+    float* rhs = S.rhs.f();
+    GPB_TRY(k_copy(rhs, cross.f(), (int64_t)m * E.nl, st));
+    float* norms_dev = S.scal.f() + 3 * m;
+    GPB_TRY(column_norms(E, rhs, m, norms, norms_dev, true));
+    CGResult cg;
+    GPB_TRY(cg_solve(E, precond_rank > 0 ? &P : nullptr, S, rhs, m, max_cg_iter, 0, cg_tol, false,
+                     cg));
+    total_iters += cg.iters;
+    float* sol = S.x.f();
+    GPB_TRY(k_scale_cols(sol, E.nl, E.nl, m, norms_dev, 0, st));
+    // 3. var = max(k** - K(X, x*) . v, 1e-10) + noise.
+    const float* a[1] = {cross.f()};
+    const float* bb[1] = {sol};
+    GPB_TRY(E.coldots(1, a, bb, E.nl, m, true));
+    GPB_CHECK_CUDA(cudaMemcpyAsync(dg.data(), diag.ptr, m * sizeof(float), cudaMemcpyDeviceToHost, st));
+    GPB_CHECK_CUDA(cudaStreamSynchronize(st));
+    for (int c = 0; c < m; ++c) {
+      float v = dg[c] - (float)E.host_sums[c];
+      if (v < 1e-10f) v = 1e-10f;
+      var_out[c0 + c] = v + p->noise;
+    }
+  }
+  if (cg_iters_out) *cg_iters_out = total_iters;
+  return provider_check_device_error(p);
 }
 
 }  // extern "C"

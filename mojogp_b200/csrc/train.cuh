@@ -34,6 +34,9 @@ int cg_solve(Engine& E, Precond* P, BBMMState& S, const float* rhs, int t, int m
 int bbmm_step(Engine& E, Precond* P, BBMMState& S, int num_probes, int max_cg, int max_tridiag,
               float tol, int iteration, bool recycle, BBMMResult& R);
 int k_sub_scalar(float* v, int64_t count, float s, cudaStream_t st);
+// Column 2-norms over all ranks (host and device copies); normalises in place.
+int column_norms(Engine& E, float* v, int t, std::vector<float>& norms_h, float* norms_dev,
+                 bool normalize);
 // (K + noise) x = y by CG with the relative-residual stop (predict.cu).
 int alpha_cg(Engine& E, const float* y_local, float* x, int max_iter, float tol, int* iters_out);
 // LMC gradients from the BBMM solution (lmc.cu); sol holds [alpha | scaled

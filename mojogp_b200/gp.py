@@ -259,13 +259,15 @@ class SingleOutputGP:
     def predict(self, X_test, return_std: bool = False, return_var: bool = False,
                 variance_method: str = "love", max_cg_iterations: Optional[int] = None,
                 cg_tolerance: Optional[float] = None,
-                max_root_decomposition_size: Optional[int] = None):
-        """Predictive mean (and LOVE variance / std, including the noise term)."""
+                max_root_decomposition_size: Optional[int] = None,
+                preconditioner_rank: Optional[int] = None,
+                exact_prediction_block_cols: Optional[int] = None):
+        """Predictive mean and variance / std including the noise term: LOVE
+        (variance_method="love"), CG-exact ("exact") or none ("mean_only")."""
         if not self._is_trained:
             raise RuntimeError("GP must be trained first.")
-        if variance_method not in ("love", "mean_only"):
-            raise NotImplementedError(
-                f"variance_method={variance_method!r}: this build implements 'love' and 'mean_only'")
+        if variance_method not in ("love", "exact", "mean_only"):
+            raise ValueError("variance_method must be one of 'love', 'exact', 'mean_only'")
         Xt = np.ascontiguousarray(X_test, dtype=np.float32)
         if Xt.ndim == 1:
             Xt = Xt[:, None]
@@ -279,6 +281,17 @@ class SingleOutputGP:
             mean, var = cache.predict_sharded(Xt, self._comm, return_var=want_var)
         else:
             mean, var = cache.predict(Xt, return_var=want_var)
+        if variance_method == "exact":
+            # predict_variance_exact_jit defaults: 300 iterations, tol 1e-3, the
+            # training preconditioner rank (gp.py:85-86).
+            from .prediction import exact_variance
+            rank = preconditioner_rank if preconditioner_rank is not None else \
+                int(self._train_info.get("precond_rank", 0))
+            var, _ = exact_variance(
+                self._provider, Xt,
+                max_cg_iter=max_cg_iterations if max_cg_iterations is not None else 300,
+                cg_tol=cg_tolerance if cg_tolerance is not None else 1e-3,
+                precond_rank=rank, block_cols=exact_prediction_block_cols or 0, comm=self._comm)
         if var is None:
             var = np.zeros_like(mean)
         std = np.sqrt(np.maximum(var, 0))

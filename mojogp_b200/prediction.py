@@ -30,6 +30,21 @@ def compute_alpha(provider: Provider, y_centered: np.ndarray, max_cg_iter: int =
     return alpha, int(it.value)
 
 
+def exact_variance(provider: Provider, X_test: np.ndarray, max_cg_iter: int = 300,
+                   cg_tol: float = 1e-3, precond_rank: int = 0, block_cols: int = 0, comm=None):
+    """CG-exact predictive variance (noise included) for every test point; returns
+    (variance [m], total CG iterations over the blocks)."""
+    Xt = np.ascontiguousarray(X_test, dtype=np.float32)
+    if Xt.ndim == 1:
+        Xt = Xt[:, None]
+    var = np.zeros(Xt.shape[0], np.float32)
+    it = C.c_int32()
+    _lib.call("gpb_predict_exact_variance", provider.h, C.c_void_p(comm.handle) if comm else None,
+              _p(Xt), Xt.shape[0], int(block_cols), int(max_cg_iter), float(cg_tol),
+              int(precond_rank), _p(var), C.byref(it))
+    return var, it.value
+
+
 class PredictionCache:
     """Device-resident alpha and LOVE root S ([rank][n]) for repeated predictions."""
 

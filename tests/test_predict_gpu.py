@@ -74,3 +74,46 @@ def test_mean_only_cache(gpb_lib):
     from oracle import kernels as ok
     ref = ok.kernel_matrix(RBF().to_spec(d), np.array([0.5, 1.0]), X[:10], X) @ alpha + 0.5
     np.testing.assert_allclose(mu, ref, rtol=1e-5, atol=1e-5)
+
+
+@pytest.mark.parametrize("rank,block", [(0, 0), (20, 37)])
+def test_exact_variance_vs_dense(gpb_lib, rank, block):
+    """CG-exact variance (predict_variance_exact_jit) against the dense formula
+    k** - k*^T (K + noise I)^{-1} k* + noise; ragged blocks of 37 test points."""
+    from oracle import kernels as ok
+    rng = np.random.default_rng(8)
+    n, d, nt = 700, 3, 100
+    X = rng.uniform(0, 1, size=(n, d)).astype(np.float32)
+    Xs = rng.uniform(-0.1, 1.1, size=(nt, d)).astype(np.float32)
+    k = make_ard_kernel(RBF(ard=True), d)
+    p = np.array([0.4, 0.6, 0.8, 1.2], np.float32)
+    noise = 0.05
+    prov = Provider(X, k, p, noise)
+    var, iters = prediction.exact_variance(prov, Xs, max_cg_iter=1000, cg_tol=1e-6,
+                                           precond_rank=rank, block_cols=block)
+    spec = k.to_spec(d)
+    K = ok.kernel_matrix(spec, p, X.astype(np.float64))
+    Kx = ok.kernel_matrix(spec, p, Xs.astype(np.float64), X.astype(np.float64))
+    kss = np.diag(ok.kernel_matrix(spec, p, Xs.astype(np.float64)))
+    ref = np.maximum(kss - np.einsum("ij,ji->i", Kx, np.linalg.solve(K + noise * np.eye(n), Kx.T)),
+                     1e-10) + noise
+    assert iters > 0
+    np.testing.assert_allclose(var, ref, rtol=1e-3, atol=1e-5)
+
+
+def test_gp_predict_exact_route(gpb_lib):
+    from mojogp_b200.gp import SingleOutputGP
+    rng = np.random.default_rng(2)
+    X = np.linspace(-3, 3, 400, dtype=np.float32)[:, None]
+    y = (np.sin(2 * X[:, 0]) + 0.05 * rng.standard_normal(400)).astype(np.float32)
+    gp = SingleOutputGP(RBF())
+    gp.fit(X, y, max_iterations=10, method="matrix_free")
+    Xs = np.linspace(-4, 4, 64, dtype=np.float32)[:, None]
+    m_e, v_e = gp.predict(Xs, return_var=True, variance_method="exact", cg_tolerance=1e-5)
+    m_l, v_l = gp.predict(Xs, return_var=True, variance_method="love",
+                          max_root_decomposition_size=400, cg_tolerance=1e-5)
+    # same alpha solve settings: the mean does not depend on the variance route
+    np.testing.assert_allclose(m_e, m_l, rtol=0, atol=1e-6)
+    np.testing.assert_allclose(v_e, v_l, rtol=2e-2, atol=1e-4)
+    with pytest.raises(ValueError):
+        gp.predict(Xs, variance_method="bogus")
