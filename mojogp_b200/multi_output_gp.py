@@ -358,3 +358,277 @@ class MultiOutputLMCGP:
         if return_std:
             return mean, np.sqrt(var)
         return mean, var
+
+
+def _icm_initial_W(T: int, R: int, seed: int = 42) -> np.ndarray:
+    """Initial low-rank task factor W [T, R] in [0.1, 0.5] from the reference's
+    counter-hash (kernels/task_covariance.mojo:168-205): the same numbers, so a
+    fit starts from the reference's state."""
+    W = np.empty(T * R, np.float32)
+    for i in range(T * R):
+        state = (seed ^ ((i * 2654435761) & 0xFFFFFFFFFFFFFFFF)) & 0xFFFFFFFFFFFFFFFF
+        state = (state * 1103515245 + 12345) & 0x7FFFFFFF
+        W[i] = np.float32(0.1) + np.float32(np.float32(state) / np.float32(0x7FFFFFFF)) * np.float32(0.4)
+    return W.reshape(T, R)
+
+
+class MultiOutputGP:
+    """Multi-output GP with ICM task covariance, matrix-free on B200.
+
+    Mirrors the reference's MultiOutputGP (mojogp/multi_output_gp.py:859-2520)
+    and train_multi_output_jit (kernels/jit/jit_multi_output.mojo:128-817):
+      K_full = os * (B (x) K_X) + diag(noise_t (x) 1_n),  B = W W^T + diag(softplus(raw_v)),
+    i.e. the LMC operator with one latent kernel and A = os * B, trained by BBMM
+    with the sum-of-Kronecker preconditioner (KroneckerPreconditioner is its R = 1
+    case). Prediction follows predict_multi_output
+    (jit_engine_multi_output_bindings.mojo:329-545): with os * B = Q Lambda Q^T
+    (Lambda clamped at 1e-6) and mean task noise s2, the latent variance is
+    sum_s Q[t, s]^2 lambda_s var_s(x*), var_s the posterior variance of K_X with
+    noise s2 / lambda_s (LOVE or exact CG); the mean is K(X*, X) alpha (os B)^T + mean_t.
+    """
+
+    _PRESETS = {
+        "fast": dict(max_cg_iter=50, cg_tol=5e-2, num_probes=5, max_tridiag_iter=15,
+                     precond_rank=5, precond_rebuild_threshold=0.75),
+        "balanced": dict(max_cg_iter=200, cg_tol=1e-2, num_probes=10, max_tridiag_iter=30,
+                         precond_rank=15, precond_rebuild_threshold=0.5),
+        "accurate": dict(max_cg_iter=400, cg_tol=1e-2, num_probes=20, max_tridiag_iter=60,
+                         precond_rank=20, precond_rebuild_threshold=0.25),
+    }
+
+    def __init__(self, kernel="rbf", task_rank: int = -1, ard: bool = False,
+                 num_probes: Optional[int] = None, max_cg_iterations: Optional[int] = None,
+                 cg_tolerance: Optional[float] = None, preconditioner_rank: Optional[int] = None,
+                 precond_rebuild_threshold: Optional[float] = None,
+                 use_preconditioner: Optional[bool] = None, init_mean=None,
+                 preset: Optional[str] = None, max_tridiag_iterations: Optional[int] = None,
+                 device: int = 0):
+        if preset is not None and preset not in self._PRESETS:
+            raise ValueError(f"Unknown preset '{preset}'. Must be one of: {list(self._PRESETS)}")
+        base = dict(self._PRESETS[preset or "balanced"])
+        for key, val in (("num_probes", num_probes), ("max_cg_iter", max_cg_iterations),
+                         ("cg_tol", cg_tolerance), ("precond_rank", preconditioner_rank),
+                         ("precond_rebuild_threshold", precond_rebuild_threshold),
+                         ("max_tridiag_iter", max_tridiag_iterations)):
+            if val is not None:
+                base[key] = val
+        if use_preconditioner is False:
+            base["precond_rank"] = 0
+        if isinstance(kernel, str):
+            if kernel.lower() not in _STR:
+                raise ValueError(f"Unknown kernel '{kernel}'. Must be one of: {list(_STR)}")
+            kernel = _STR[kernel.lower()]()
+        if not isinstance(kernel, KernelNode):
+            raise ValueError(f"kernel must be a KernelNode or a kernel string, got {type(kernel)}")
+        self.kernel = kernel
+        self.task_rank = int(task_rank)
+        self.ard = ard
+        self.num_probes = int(base["num_probes"])
+        self.max_cg_iter = int(base["max_cg_iter"])
+        self.cg_tol = float(base["cg_tol"])
+        self.max_tridiag_iter = int(base["max_tridiag_iter"])
+        self.precond_rank = int(base["precond_rank"])
+        self.precond_rebuild_threshold = float(base["precond_rebuild_threshold"])
+        self.init_mean = init_mean
+        self.device = device
+        self._lmc: Optional[LMC] = None
+
+    # ------------------------------------------------------------------ fit
+    def fit(self, X, Y, max_iterations: int = 100, learning_rate: float = 0.05,
+            method: str = "matrix_free", initial_noise: float = 0.1,
+            initial_noise_per_task=None, verbose: bool = False, early_stop_tol: float = 1e-4,
+            early_stop_patience: int = 15, comm=None):
+        if method not in ("matrix_free", "mf", "auto"):
+            raise NotImplementedError(f"method={method!r}: this build implements matrix-free ICM")
+        X = np.ascontiguousarray(X, np.float32)
+        if X.ndim == 1:
+            X = X[:, None]
+        Y = np.asarray(Y, np.float32)
+        if Y.ndim != 2 or Y.shape[0] != X.shape[0]:
+            raise ValueError("Y must be [n, T] with the rows of X")
+        n, d = X.shape
+        T = Y.shape[1]
+        R = T if self.task_rank < 0 else self.task_rank
+        if R < 1 or R > T:
+            raise ValueError(f"task_rank must be -1 or in [1, {T}]")
+        self.T, self.dim, self._X = T, d, X
+        self.kernel_resolved = make_ard_kernel(self.kernel, d) if self.ard else \
+            self.kernel.resolve_ard(d)
+        params0 = np.asarray(self.kernel_resolved.get_initial_params(), np.float32)
+        mask = np.asarray(self.kernel_resolved.engine_trainable_mask(), bool)
+        prov = Provider(X, self.kernel_resolved, params0, 0.0, device=self.device)
+        self._lmc = LMC([prov], T, comm=comm)
+        raw_p = np.array([_isp(float(v)) for v in params0])
+        raw_os = _isp(1.0)
+        noise0 = (np.full(T, initial_noise) if initial_noise_per_task is None
+                  else np.asarray(initial_noise_per_task, np.float64))
+        raw_noise = np.array([_isp(float(v)) for v in noise0])
+        if self.init_mean is None:
+            raw_mean = Y.mean(axis=0).astype(np.float64)
+        else:
+            raw_mean = np.broadcast_to(np.asarray(self.init_mean, np.float64), (T,)).copy()
+        W = _icm_initial_W(T, R).astype(np.float64)
+        raw_v = np.zeros(T)
+        P = len(raw_p)
+        m = np.zeros(P + 1 + T + T * R + T + T)
+        v = np.zeros_like(m)
+        lr = learning_rate
+        t_step = 1
+
+        def adam(idx, g):
+            m[idx] = 0.9 * m[idx] + 0.1 * g
+            v[idx] = 0.999 * v[idx] + 0.001 * g * g
+            mh = m[idx] / (1 - 0.9 ** t_step)
+            vh = v[idx] / (1 - 0.999 ** t_step)
+            return -lr * mh / (math.sqrt(vh) + 1e-8)
+
+        Yb = Y.T.astype(np.float64)
+        hist, cg_hist = [], []
+        best, best_nll, patience = None, 1e30, 0
+        es_best = 1e30  # early-stopping tracker, separate from the best state
+        last = None
+        self.precond_rebuild_count = 0
+        converged = False
+        for it in range(max_iterations):
+            params = np.array([_sp(r) for r in raw_p], np.float32)
+            prov.update_params(params)
+            os_ = _sp(raw_os)
+            noise = np.array([_sp(r) for r in raw_noise])
+            B = W @ W.T + np.diag([_sp(r) for r in raw_v])
+            self._lmc.set_coregion((os_ * B)[None].astype(np.float32), noise)
+            state = (np.concatenate([params, [os_], noise, B.ravel()]))
+            if self.precond_rank > 0:
+                rebuild = last is None or np.max(np.abs(state - last) /
+                                                 (np.abs(last) + 1e-8)) > self.precond_rebuild_threshold
+                if rebuild:
+                    if last is not None:
+                        self.precond_rebuild_count += 1
+                    self._lmc.build_precond(self.precond_rank)
+                    last = state
+            yc = (Yb - raw_mean[:, None]).astype(np.float32)
+            res = self._lmc.bbmm(yc, self.num_probes, self.max_cg_iter, self.max_tridiag_iter,
+                                 self.cg_tol, it, it > 0)
+            if res["cg_iters"] >= self.max_cg_iter and self.precond_rank > 0:
+                # jit_multi_output.mojo: rebuild the preconditioner and retry once
+                self._lmc.build_precond(self.precond_rank)
+                last = state
+                self.precond_rebuild_count += 1
+                res = self._lmc.bbmm(yc, self.num_probes, self.max_cg_iter, self.max_tridiag_iter,
+                                     self.cg_tol, it, False)
+            nll = res["nll"]
+            hist.append(nll)
+            cg_hist.append(res["cg_iters"])
+            cg_ok = res["cg_iters"] < self.max_cg_iter
+            if (cg_ok or best is None) and np.isfinite(nll) and nll < best_nll:
+                best_nll = nll
+                best = (raw_p.copy(), raw_os, raw_noise.copy(), raw_mean.copy(), W.copy(),
+                        raw_v.copy(), res["alpha"].copy())
+            if not cg_ok:
+                break  # stop with the best valid state (jit_multi_output.mojo)
+            gA = res["gA"][0]
+            G_B = np.clip(os_ * gA, -10.0, 10.0)
+            sig = lambda x: 1.0 / (1.0 + math.exp(-x))
+            idx = 0
+            for q in range(P):
+                if mask[q]:
+                    raw_p[q] += adam(idx, res["kgrads"][q] * sig(raw_p[q]))
+                idx += 1
+            g_os = float(np.sum(gA * B))  # dNLL/dos through A = os B
+            raw_os += adam(idx, g_os * sig(raw_os))
+            idx += 1
+            for t in range(T):
+                raw_noise[t] += adam(idx, res["gnoise"][t] * sig(raw_noise[t]))
+                idx += 1
+            gW = 2.0 * G_B @ W
+            for s in range(T):
+                for r in range(R):
+                    W[s, r] += adam(idx, gW[s, r])
+                    idx += 1
+            for t in range(T):
+                raw_v[t] += adam(idx, G_B[t, t] * sig(raw_v[t]))
+                idx += 1
+            for t in range(T):
+                g = float(np.clip(-res["sum_alpha"][t] / (n * T), -100.0, 100.0))
+                raw_mean[t] += adam(idx, g)
+                idx += 1
+            t_step += 1
+            if verbose and (it % 10 == 0 or it == max_iterations - 1):
+                print(f"MO Iter {it}: NLL = {nll}")
+            if early_stop_tol > 0:
+                if nll < es_best - early_stop_tol:
+                    es_best = nll
+                    patience = 0
+                else:
+                    patience += 1
+                    if patience >= early_stop_patience:
+                        converged = True
+                        break
+        raw_p, raw_os, raw_noise, raw_mean, W, raw_v, alpha = best
+        self.params_ = np.array([_sp(r) for r in raw_p], np.float32)
+        prov.update_params(self.params_)
+        self.outputscale_ = _sp(raw_os)
+        self.noise_per_task = np.array([_sp(r) for r in raw_noise])
+        self.mean_ = raw_mean
+        self.W_ = W
+        Bs = self.outputscale_ * (W @ W.T + np.diag([_sp(r) for r in raw_v]))
+        self.task_covariance = Bs
+        self._lmc.set_coregion(Bs[None].astype(np.float32), self.noise_per_task)
+        ev, Q = np.linalg.eigh(Bs)
+        self._Lambda = np.maximum(ev, 1e-6)
+        self._Q = Q
+        self._alpha = alpha
+        self.nll_history = np.array(hist)
+        self.cg_iterations_history = cg_hist
+        self.final_nll = best_nll
+        self.converged = converged
+        return self
+
+    def log_marginal_likelihood(self) -> float:
+        return -float(self.final_nll)
+
+    # ------------------------------------------------------------ predict
+    def predict(self, X_test, return_var: bool = False, return_std: bool = False,
+                variance_method: str = "love", lanczos_rank: int = 0):
+        if self._lmc is None:
+            raise RuntimeError("model must be fit first")
+        if variance_method not in ("love", "exact", "mean_only"):
+            raise ValueError("variance_method must be one of 'love', 'exact', 'mean_only'")
+        Xt = np.ascontiguousarray(X_test, np.float32)
+        if Xt.ndim == 1:
+            Xt = Xt[:, None]
+        T, n = self.T, self._X.shape[0]
+        prov = self._lmc.providers[0]
+        alpha = self._alpha.reshape(T, n).T
+        Cs = prov.cross_matvec_host(Xt, alpha)  # [m, T]
+        mean = (Cs @ self.task_covariance.T + self.mean_[None, :]).astype(np.float32)
+        if not (return_var or return_std) or variance_method == "mean_only":
+            return mean if not (return_var or return_std) else (mean, np.zeros_like(mean))
+        from .gp import _DEFAULT_PREDICT_LANCZOS_RANK
+        from .prediction import PredictionCache, exact_variance
+        s2 = float(np.mean(self.noise_per_task))
+        rank = lanczos_rank or max(_DEFAULT_PREDICT_LANCZOS_RANK,
+                                   200 if self.kernel_resolved.has_ard() else 0)
+        rank = min(rank, n)
+        var = np.zeros((Xt.shape[0], T))
+        try:
+            for s in range(T):
+                lam = float(self._Lambda[s])
+                if lam <= 1e-8:
+                    continue
+                nz = s2 / lam
+                prov.update_noise(nz)
+                if variance_method == "love":
+                    cache = PredictionCache(prov, np.zeros(n, np.float32), 0.0, rank)
+                    _, v_s = cache.predict(Xt, return_var=True)
+                    cache.destroy()
+                else:
+                    v_s, _ = exact_variance(prov, Xt, max_cg_iter=self.max_cg_iter,
+                                            cg_tol=min(self.cg_tol, 1e-2), precond_rank=self.precond_rank)
+                latent = np.maximum(v_s.astype(np.float64) - nz, 1e-10)
+                var += (self._Q[:, s] ** 2 * lam)[None, :] * latent[:, None]
+        finally:
+            prov.update_noise(0.0)
+        var = np.maximum(var, 0).astype(np.float32)
+        if return_std:
+            return mean, np.sqrt(var)
+        return mean, var
