@@ -140,9 +140,12 @@ class SingleOutputGP:
             raise ValueError("cannot fit on an empty dataset")
         if not (np.all(np.isfinite(X)) and np.all(np.isfinite(y))):
             raise ValueError("X and y must be finite")
-        if method not in ("auto", "matrix_free"):
-            raise NotImplementedError(
-                f"method={method!r}: this build implements the matrix-free route only")
+        if method not in ("auto", "matrix_free", "mf", "materialized", "mat"):
+            raise ValueError(f"method={method!r}: expected 'auto', 'matrix_free' or 'materialized'")
+        # The materialized route (dense K + GEMM for n <= ~4e4) is served by the
+        # matrix-free tile kernels: re-evaluating K on the tensor cores costs less
+        # than streaming a stored K from HBM at t = 16 (fn_ptr_module.py:363-421).
+        self._training_method = method
         if lr_schedule not in ("constant", "cosine"):
             raise ValueError("lr_schedule must be 'constant' or 'cosine'")
         n, dim = X.shape

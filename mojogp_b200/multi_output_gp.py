@@ -179,8 +179,9 @@ class MultiOutputLMCGP:
     def fit(self, X, Y, max_iterations: int = 100, learning_rate: float = 0.05,
             initial_noise: float = 0.1, method: str = "matrix_free", verbose: bool = False,
             comm=None):
-        if method not in ("matrix_free", "auto"):
-            raise NotImplementedError(f"method={method!r}: this build implements matrix-free LMC")
+        if method not in ("matrix_free", "mf", "auto", "materialized", "mat"):
+            raise ValueError(f"method={method!r}: expected 'matrix_free' or 'materialized'")
+        # "materialized" is served by the matrix-free operator (see SingleOutputGP.fit).
         X = np.ascontiguousarray(X, np.float32)
         if X.ndim == 1:
             X = X[:, None]
@@ -435,11 +436,12 @@ class MultiOutputGP:
 
     # ------------------------------------------------------------------ fit
     def fit(self, X, Y, max_iterations: int = 100, learning_rate: float = 0.05,
-            method: str = "matrix_free", initial_noise: float = 0.1,
+            method: str = "materialized", initial_noise: float = 0.1,
             initial_noise_per_task=None, verbose: bool = False, early_stop_tol: float = 1e-4,
             early_stop_patience: int = 15, comm=None):
-        if method not in ("matrix_free", "mf", "auto"):
-            raise NotImplementedError(f"method={method!r}: this build implements matrix-free ICM")
+        if method not in ("matrix_free", "mf", "auto", "materialized", "mat"):
+            raise ValueError(f"method={method!r}: expected 'matrix_free' or 'materialized'")
+        # "materialized" is served by the matrix-free operator (see SingleOutputGP.fit).
         X = np.ascontiguousarray(X, np.float32)
         if X.ndim == 1:
             X = X[:, None]

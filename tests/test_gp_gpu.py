@@ -68,7 +68,18 @@ def test_input_validation(gpb_lib):
         gp.fit(np.zeros((5, 2)), np.zeros(4))
     with pytest.raises(ValueError):
         gp.fit(np.zeros((5, 2)), np.zeros((5, 1)))
-    with pytest.raises(NotImplementedError):
-        gp.fit(np.zeros((5, 2)), np.zeros(5), method="materialized")
+    with pytest.raises(ValueError):
+        gp.fit(np.zeros((5, 2)), np.zeros(5), method="bogus")
     with pytest.raises(RuntimeError):
         gp.predict(np.zeros((3, 2)))
+
+
+def test_materialized_route_name_is_served(gpb_lib):
+    """method="materialized" (the reference's dense route) runs the matrix-free
+    kernels and gives the same fit."""
+    rng = np.random.default_rng(4)
+    X = rng.uniform(-2, 2, size=(300, 2)).astype(np.float32)
+    y = (np.sin(X[:, 0]) + 0.1 * rng.standard_normal(300)).astype(np.float32)
+    a = SingleOutputGP(RBF()).fit(X, y, max_iterations=5, method="materialized")
+    b = SingleOutputGP(RBF()).fit(X, y, max_iterations=5, method="matrix_free")
+    np.testing.assert_allclose(a.nll_history, b.nll_history, rtol=0, atol=0)
