@@ -12,6 +12,7 @@
 #include <vector>
 
 #include "provider.cuh"
+#include "gradient_gram.cuh"
 
 namespace gpb {
 
@@ -391,6 +392,113 @@ int bilinear_generic_dp(int DP, int T, const float* xrow, const float* a, int64_
   return GPB_ERR_UNSUPPORTED;
 }
 
+// ------------------------------------------------- tensor-core RBF reduction
+// Column tiles for gb_kernel: the Gram K.V B part, b (columns col0 .. col0 +
+// ncol - 1 of the 16, the others zero) split into tf32 hi / lo, and
+// B' = [1 | z | z^2] hi / lo along N (gradient_gram.cuh).
+__global__ void pack_gb_kernel(const float* __restrict__ xs, int DP, const float* __restrict__ b,
+                               int64_t b_ld, int col0, int ncol, int64_t n, int64_t npad,
+                               float* __restrict__ dst) {
+  const int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (j >= npad) return;
+  float* base = dst + (j / 128) * gb_tile_floats(DP);
+  const int jt = (int)(j % 128);
+  const int KA = gram_kaug(DP);
+  const bool live = j < n;
+  float y[16];
+  for (int q = 0; q < DP; ++q) y[q] = live ? xs[j * DP + q] : 0.f;
+  for (int q = 0; q < DP; ++q) {
+    const float bv = -2.f * y[q];
+    const float hi = tf32_hi(bv);
+    base[gram_xoff(jt, q)] = hi;
+    base[128 * KA + gram_xoff(jt, q)] = bv - hi;
+  }
+  float e[8] = {1.f, 1.f, 1.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  gram_split3(gram_sqnorm(y, DP), e[3], e[4], e[5]);
+  for (int q = 0; q < 8; ++q) base[gram_xoff(jt, DP + q)] = e[q];
+  float* bb = base + gb_b_offset(DP);
+  for (int c = 0; c < 16; ++c) {
+    const float v = (live && c >= col0 && c < col0 + ncol) ? b[(int64_t)c * b_ld + j] : 0.f;
+    const float hi = tf32_hi(v);
+    bb[gram_xoff(jt, c)] = hi;
+    bb[2048 + gram_xoff(jt, c)] = v - hi;
+  }
+  float* bp = base + gb_bp_offset(DP) + (jt / 8) * (8 * kGBN);
+  const int k = jt % 8;
+  for (int nn = 0; nn < 40; ++nn) {
+    float f = 0.f;
+    if (live) {
+      if (nn == 0)
+        f = 1.f;
+      else if (nn <= DP)
+        f = y[nn - 1];
+      else if (nn <= 2 * DP)
+        f = y[nn - 1 - DP] * y[nn - 1 - DP];
+    }
+    const float hi = tf32_hi(f);
+    bp[gb_bp_off(nn, k)] = hi;
+    bp[gb_bp_off(40 + nn, k)] = f - hi;
+  }
+}
+
+bool gb_disabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("GPB_GRAD_TC");
+    v = (e && e[0] == '0') ? 1 : 0;
+  }
+  return v == 1;
+}
+
+// One pass (data or probe columns) of the tensor-core reduction; adds the
+// DP + 2 accumulators to acc_half.
+template <int DP>
+int gb_pass(gpb_provider* p, const float* xrow, const float* a, int64_t nrow, int64_t a_ld,
+            const float* b, int col0, int ncol, double* acc_half, cudaStream_t st) {
+  constexpr int NACC = DP + 2;
+  const int64_t npad = round_up(std::max<int64_t>(p->n, 1), kJT);
+  const int ntiles = (int)(npad / kJT);
+  void* xv = nullptr;
+  GPB_TRY(p->ws.get(WS_XV, (size_t)ntiles * gb_tile_floats(DP) * sizeof(float), &xv));
+  pack_gb_kernel<<<(unsigned)ceil_div(npad, 128), 128, 0, st>>>(p->Xs_d, DP, b, p->n, col0, ncol,
+                                                               p->n, npad, (float*)xv);
+  GPB_CHECK_CUDA(cudaGetLastError());
+  auto kern = gb_kernel<DP>;
+  const size_t smem = (size_t)kGBStages * gb_tile_floats(DP) * sizeof(float);
+  static bool init = false;
+  static int sms = 148;
+  if (!init) {
+    GPB_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    int dev = 0, res = 0;
+    GPB_CHECK_CUDA(cudaGetDevice(&dev));
+    GPB_CHECK_CUDA(cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev));
+    GPB_CHECK_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&res, kern, kGBThreads, smem));
+    // The kernel allocates all 512 TMEM columns: two CTAs must never share an SM.
+    GPB_REQUIRE(res == 1, GPB_ERR_UNSUPPORTED, "gradient tile kernel: %d CTAs per SM", res);
+    init = true;
+  }
+  const int64_t row_blocks = ceil_div(nrow, kGBEpi);
+  int splits = kv_choose_splits(row_blocks, ntiles, 1, sms);
+  const int tps = (int)ceil_div(ntiles, splits);
+  splits = (int)ceil_div(ntiles, tps);
+  const int64_t nb = row_blocks * splits;
+  void* part = nullptr;
+  GPB_TRY(p->ws.get(WS_GRAD, (size_t)nb * NACC * sizeof(float) + 4096, &part));
+  kern<<<dim3((unsigned)row_blocks, (unsigned)splits), kGBThreads, smem, st>>>(
+      xrow, a, nrow, a_ld, col0, ncol, (const float*)xv, ntiles, tps, (float*)part, p->err_d);
+  GPB_CHECK_CUDA(cudaGetLastError());
+  p->launches += 2;
+  void* sums = nullptr;
+  GPB_TRY(p->ws.get(WS_MISC, (size_t)NACC * sizeof(double), &sums));
+  sum_partials_kernel<<<1, 128, 0, st>>>((float*)part, nb, NACC, (double*)sums);
+  GPB_CHECK_CUDA(cudaGetLastError());
+  double tmp[NACC];
+  GPB_CHECK_CUDA(cudaMemcpyAsync(tmp, sums, NACC * sizeof(double), cudaMemcpyDeviceToHost, st));
+  GPB_CHECK_CUDA(cudaStreamSynchronize(st));
+  for (int q = 0; q < NACC; ++q) acc_half[q] += tmp[q];
+  return GPB_OK;
+}
+
 // Sum over row range [row_begin, row_end) of the bilinear forms; results are
 // accumulated (added) into data_out/trace_out (P doubles each, host).
 int provider_bilinear_rows(gpb_provider* p, const float* a_dev, int64_t a_ld, const float* b_dev,
@@ -415,7 +523,24 @@ int provider_bilinear_rows_nd(gpb_provider* p, const float* a_dev, int64_t a_ld,
   // Generic evaluator reads raw (unscaled) inputs: its plan's prescale is identity.
   const float* xrow = p->Xs_d + row_begin * p->DP;
   std::vector<double> acc(nacc, 0.0), tmp(nacc);
-  for (int64_t c0 = 0; c0 < ncols; c0 += 16) {
+  // Tensor-core route: RBF on the Gram path (bounded prescaled norms), one
+  // pass for the data columns and one for the probe columns of each chunk.
+  const bool tc = p->eval == GPB_KERNEL_RBF && p->gram_ok && (p->DP == 8 || p->DP == 16) &&
+                  !kv_tc_disabled() && !gb_disabled();
+  for (int64_t c0 = 0; tc && c0 < ncols; c0 += 16) {
+    const int tcols = (int)std::min<int64_t>(ncols - c0, 16);
+    const int nd = (int)std::max<int64_t>(0, std::min<int64_t>(ndata - c0, tcols));
+    const float* a_chunk = a_dev + c0 * a_ld;
+    const float* b_chunk = b_dev + c0 * p->n;
+    for (int half = 0; half < 2; ++half) {
+      const int col0 = half == 0 ? 0 : nd, nc = half == 0 ? nd : tcols - nd;
+      if (nc <= 0) continue;
+      double* dst = acc.data() + half * (p->DP + 2);
+      GPB_TRY(p->DP == 8 ? gb_pass<8>(p, xrow, a_chunk, nrow, a_ld, b_chunk, col0, nc, dst, st)
+                         : gb_pass<16>(p, xrow, a_chunk, nrow, a_ld, b_chunk, col0, nc, dst, st));
+    }
+  }
+  for (int64_t c0 = 0; !tc && c0 < ncols; c0 += 16) {
     const int64_t rem = ncols - c0;
     const int T = rem > 4 ? 16 : 4;
     const int tcols = (int)std::min<int64_t>(rem, T);

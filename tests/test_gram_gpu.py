@@ -100,3 +100,25 @@ def test_gram_rows_and_cross(gpb_lib):
     got = prov.cross_matvec_host(Xt, V)
     ref = ok.cross_matvec(k.to_spec(16), p, Xt, X, V)
     assert rel_fro(got, ref) < 1e-5
+
+
+@pytest.mark.parametrize("kname,n,d,t", [("rbf_ard", 3000, 16, 16), ("rbf_iso", 1000, 8, 11),
+                                         ("rbf_ard", 777, 5, 20)])
+def test_gram_gradient_bilinear_vs_oracle(gpb_lib, kname, n, d, t):
+    """Tensor-core RBF gradient reduction (gradient_gram.cuh) against the
+    float64 oracle: data column 0, probe columns 1.. (two chunks when t > 16)."""
+    rng = np.random.default_rng(n + t)
+    k = make_ard_kernel(RBF(ard=True), d) if kname == "rbf_ard" else RBF()
+    kk = k.resolve_ard(d)
+    p = np.array([rng.uniform(0.8, 2.0) for _ in range(kk.num_params())], np.float32)
+    X = rng.standard_normal((n, d)).astype(np.float32)
+    A = rng.standard_normal((n, t)).astype(np.float32)
+    B = rng.standard_normal((n, t)).astype(np.float32)
+    prov = Provider(X, k, p, 0.1)
+    assert prov.matvec_layout(16) == "gram-tensor-core"
+    ad = DeviceBuffer.from_host(np.ascontiguousarray(A.T))
+    bd = DeviceBuffer.from_host(np.ascontiguousarray(B.T))
+    data, trace = prov.gradient_bilinear(ad, bd, t)
+    rd, rt = ok.gradient_bilinear(k.to_spec(d), p, X, A, B)
+    np.testing.assert_allclose(data, rd, rtol=1e-4, atol=1e-4 * np.abs(rd).max())
+    np.testing.assert_allclose(trace, rt, rtol=1e-4, atol=1e-4 * np.abs(rt).max())
