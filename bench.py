@@ -49,7 +49,7 @@ def parse():
     ap.add_argument("--rhs", dest="t", type=int, default=16)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
-    ap.add_argument("--fit-iters", type=int, default=1,
+    ap.add_argument("--fit-iters", type=int, default=3,
                     help="outer fit iterations timed for fit s/iter (0 = skip)")
     return ap.parse_args()
 
@@ -226,7 +226,7 @@ def main():
         fit = {"s_per_iter": it_s, "iters_timed": int(args.fit_iters),
                "cg_iters_per_iter": [int(c) for c in res["cg_iterations_history"]],
                "num_probes": 15, "precond_rank": 0,
-               "note": "median host wall time per outer iteration (probes, mBCG capped at 30 "
+               "note": "median host wall time per outer iteration over the timed iterations (probes, mBCG capped at 30 "
                        "iterations = max_tridiag, SLQ, fused gradients, Adam)"}
 
     achieved = flops_local / (kmean * 1e-3) / 1e12
