@@ -148,3 +148,30 @@ def test_lmc_predict_variance_vs_exact_latents(gpb_lib):
     ref += gp.noise[None, :]
     assert var.shape == (50, 4)
     np.testing.assert_allclose(var, ref, rtol=2e-3, atol=1e-4)
+
+
+def test_lmc_bbmm_rbf16_tensor_core_gradients(gpb_lib):
+    """RBF-ARD latent at d = 16 takes the Gram K.V kernel and the tensor-core
+    gradient reduction with T data columns; BBMM outputs against the oracle."""
+    rng = np.random.default_rng(21)
+    n, d, T = 400, 16, 3
+    X = (0.6 * rng.standard_normal((n, d))).astype(np.float32)
+    ks = [make_ard_kernel(RBF(ard=True), d), Matern32()]
+    ps = [np.concatenate([rng.uniform(1.0, 2.0, d), [1.0]]).astype(np.float32),
+          np.array([1.5, 0.7], np.float32)]
+    A = np.stack([(lambda M: 0.1 * (M @ M.T) + 0.05 * np.eye(T))(rng.normal(size=(T, T)) * 0.5)
+                  for _ in ks]).astype(np.float32)
+    noise = rng.uniform(0.5, 1.0, size=T).astype(np.float32)
+    provs = [Provider(X, k, p, 0.0) for k, p in zip(ks, ps)]
+    assert provs[0].matvec_layout(16) == "gram-tensor-core"
+    lmc = LMC(provs, T)
+    lmc.set_coregion(A, noise)
+    Y = rng.standard_normal((n, T)).astype(np.float32)
+    yc = (Y - Y.mean(0)).T.copy()
+    got = lmc.bbmm(yc, 8, 30, 30, 0.0, 2, False)
+    ref = olmc.lmc_bbmm([k.to_spec(d) for k in ks], ps, X, Y - Y.mean(0), A, noise, 8, 30, 30,
+                        0.0, iteration=2)
+    assert abs(got["nll"] - ref["nll"]) < 1e-4 * abs(ref["nll"])
+    for key in ("kgrads", "gA", "gnoise"):
+        np.testing.assert_allclose(got[key], ref[key], rtol=0,
+                                   atol=1e-3 * np.abs(ref[key]).max(), err_msg=key)
