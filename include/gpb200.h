@@ -348,6 +348,17 @@ int gpb_lmc_precond_sample(gpb_lmc* h, float* out_dev, int32_t num, uint64_t see
 int gpb_lmc_solve(gpb_lmc* h, const float* rhs_host, int32_t max_cg_iter, float cg_tol,
                   float* x_host_out, int32_t* iters_out);
 
+/* Exact LMC posterior variance (_predict_lmc_full_exact_variance_backend,
+ * mojogp/multi_output_gp.py:4360-4519): var[c][t] = max(sum_s A_s[t][t]
+ * k_s(x*_c, x*_c) - r^T K_full^{-1} r + noise_t, 1e-10) with
+ * r = sum_s k_s(X, x*_c) (x) A_s[:, t]. Test points are solved in blocks of
+ * block_cols / T points (block_cols <= 0: 512) x all T tasks by batched CG
+ * (relative stop cg_tol; the LMC preconditioner when built). xtest [n_test][d]
+ * host, var_out [n_test][T] host. Every rank of a sharded handle returns all. */
+int gpb_lmc_predict_exact_variance(gpb_lmc* h, const float* xtest_host, int64_t n_test,
+                                   int32_t block_cols, int32_t max_cg_iter, float cg_tol,
+                                   float* var_out, int32_t* cg_iters_out);
+
 /* Tensor-core self-test (no reference counterpart): one 128x16x8 tcgen05
  * kind::tf32 MMA from shared-memory operands, A [128][8], B [16][8] row-major
  * host arrays, D = A B^T [128][16]. variant 0 = the operand layout the

@@ -85,6 +85,7 @@ SIGNATURES = {
     "gpb_lmc_build_precond": [P, c_i32, PI32, P],
     "gpb_lmc_precond_apply": [P, P, P, c_i64],
     "gpb_lmc_precond_sample": [P, P, c_i32, C.c_uint64],
+    "gpb_lmc_predict_exact_variance": [P, P, c_i64, c_i32, c_i32, c_f32, P, PI32],
 }
 _RESTYPES = {"gpb_version": C.c_char_p}
 

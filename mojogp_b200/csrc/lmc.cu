@@ -496,6 +496,23 @@ int lmc_bbmm_gradients(Engine& E, BBMMState& S, float* sol, const float* rf, int
   return GPB_OK;
 }
 
+// Exact-variance right-hand sides: column (c, t) of a block of b test points
+// is sum_s k_s(X, x*_c) (x) A_s[:, t], i.e. rhs[(c T + t)][t'][i] =
+// sum_s A_s[t'][t] cross_s[c][i] (cross [R][b][nl], A [R][T][T]).
+__global__ void lmc_exact_rhs_kernel(const float* __restrict__ cross,
+                                     const float* __restrict__ A, int R, int T, int b,
+                                     int64_t nl, float* __restrict__ rhs) {
+  const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  const int col = blockIdx.y;  // c * T + t
+  const int tp = blockIdx.z;
+  if (i >= nl) return;
+  const int c = col / T, t = col % T;
+  float acc = 0.f;
+  for (int s = 0; s < R; ++s)
+    acc += A[((size_t)s * T + tp) * T + t] * cross[((int64_t)s * b + c) * nl + i];
+  rhs[((int64_t)col * T + tp) * nl + i] = acc;
+}
+
 }  // namespace gpb
 
 using namespace gpb;
@@ -661,6 +678,90 @@ int gpb_lmc_solve(gpb_lmc* h, const float* rhs_host, int32_t max_cg_iter, float 
   GPB_TRY(alpha_cg(E, y.f(), x.f(), max_cg_iter, cg_tol, &it));
   GPB_TRY(op.to_host(x.f(), x_host_out));
   if (iters_out) *iters_out = it;
+  return provider_check_device_error(op.prov[0]);
+}
+
+// Exact LMC posterior variance (_predict_lmc_full_exact_variance_backend,
+// mojogp/multi_output_gp.py:4360-4519): per test point c and output task t,
+// var = max(sum_s A_s[t][t] k_s(x*, x*) - r^T K_full^{-1} r + noise_t, 1e-10)
+// with r = sum_s k_s(X, x*_c) (x) A_s[:, t]. The reference solves one
+// right-hand side at a time; here a block of test points x all T tasks is one
+// batched CG on the LMC operator (with the sum-of-Kronecker preconditioner when
+// built), normalised columns, as the single-output exact variance.
+int gpb_lmc_predict_exact_variance(gpb_lmc* h, const float* xtest_host, int64_t n_test,
+                                   int32_t block_cols, int32_t max_cg_iter, float cg_tol,
+                                   float* var_out, int32_t* cg_iters_out) {
+  clear_error();
+  GPB_REQUIRE(h && xtest_host && var_out && n_test >= 0 && max_cg_iter >= 1, GPB_ERR_INVALID,
+              "bad arguments");
+  if (n_test == 0) return GPB_OK;
+  LmcOp& op = h->op;
+  GPB_CHECK_CUDA(cudaSetDevice(op.prov[0]->device));
+  Engine& E = op.E;
+  cudaStream_t st = E.st;
+  const int R = op.R, T = op.T, d = op.prov[0]->d;
+  for (int s = 1; s < R; ++s)
+    GPB_REQUIRE(op.prov[s]->d == d, GPB_ERR_INVALID, "latent input dims differ");
+  // Block of test points: all T task columns of each, at most 512 columns.
+  const int cap = block_cols > 0 ? block_cols : 512;
+  const int b = (int)std::min<int64_t>(n_test, std::max(1, cap / T));
+  const int mc = b * T;
+  BBMMState S;
+  GPB_TRY(S.ensure(E, mc, 1));
+  DBuf xt, cross, rhs0, diag;
+  GPB_TRY(xt.ensure((size_t)n_test * d * sizeof(float)));
+  GPB_TRY(cross.ensure((size_t)R * b * std::max<int64_t>(op.nl, 1) * sizeof(float)));
+  GPB_TRY(rhs0.ensure((size_t)mc * std::max<int64_t>(E.nl, 1) * sizeof(float)));
+  GPB_TRY(diag.ensure((size_t)R * b * sizeof(float)));
+  GPB_CHECK_CUDA(cudaMemcpyAsync(xt.ptr, xtest_host, (size_t)n_test * d * sizeof(float),
+                                 cudaMemcpyHostToDevice, st));
+  GPB_CHECK_CUDA(cudaStreamSynchronize(st));
+  std::vector<float> norms, dg((size_t)R * b);
+  int total_iters = 0;
+  for (int64_t c0 = 0; c0 < n_test; c0 += b) {
+    const int m = (int)std::min<int64_t>(b, n_test - c0);
+    const int cols = m * T;
+    const float* xb = xt.f() + c0 * d;
+    // 1. Per-latent cross blocks K_s(X_local, X*_block) and prior diagonals.
+    for (int s = 0; s < R; ++s) {
+      GPB_TRY(cross_fill(op.prov[s], op.r0, op.nl, xb, m, cross.f() + (int64_t)s * b * op.nl, st));
+      GPB_TRY(gpb_extract_diagonal_test(op.prov[s], diag.f() + (int64_t)s * b, xb, m));
+      GPB_CHECK_CUDA(cudaStreamSynchronize(op.prov[s]->stream));
+    }
+    if (op.nl > 0) {
+      dim3 grid((unsigned)ceil_div(op.nl, 128), (unsigned)cols, (unsigned)T);
+      lmc_exact_rhs_kernel<<<grid, 128, 0, st>>>(cross.f(), op.A_d.f(), R, T, b, op.nl,
+                                                   rhs0.f());
+      GPB_CHECK_CUDA(cudaGetLastError());
+    }
+    // 2. K_full V = rhs by batched CG on normalised columns.
+    float* rhs = S.rhs.f();
+    GPB_TRY(k_copy(rhs, rhs0.f(), (int64_t)cols * E.nl, st));
+    float* norms_dev = S.scal.f() + 3 * cols;
+    GPB_TRY(column_norms(E, rhs, cols, norms, norms_dev, true));
+    CGResult cg;
+    GPB_TRY(cg_solve(E, op.pc.rank > 0 ? &op.pc : nullptr, S, rhs, cols, max_cg_iter, 0, cg_tol,
+                     false, cg));
+    total_iters += cg.iters;
+    float* sol = S.x.f();
+    GPB_TRY(k_scale_cols(sol, E.nl, E.nl, cols, norms_dev, 0, st));
+    // 3. Correction r^T v per column, then the variance.
+    const float* a[1] = {rhs0.f()};
+    const float* bb[1] = {sol};
+    GPB_TRY(E.coldots(1, a, bb, E.nl, cols, true));
+    GPB_CHECK_CUDA(cudaMemcpyAsync(dg.data(), diag.ptr, (size_t)R * b * sizeof(float),
+                                   cudaMemcpyDeviceToHost, st));
+    GPB_CHECK_CUDA(cudaStreamSynchronize(st));
+    for (int c = 0; c < m; ++c)
+      for (int t = 0; t < T; ++t) {
+        double prior = 0.0;
+        for (int s = 0; s < R; ++s)
+          prior += (double)op.A[((size_t)s * T + t) * T + t] * dg[(size_t)s * b + c];
+        double v = prior - E.host_sums[c * T + t] + op.noise[t];
+        var_out[(c0 + c) * T + t] = (float)std::max(v, 1e-10);
+      }
+  }
+  if (cg_iters_out) *cg_iters_out = total_iters;
   return provider_check_device_error(op.prov[0]);
 }
 

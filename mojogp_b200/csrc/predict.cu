@@ -252,6 +252,14 @@ __global__ void cross_fill_kernel(const float* __restrict__ X, int64_t r0, int64
   }
   out[(int64_t)c * nl + i] = tree_eval<false>(K, xi, xc, nullptr);
 }
+int cross_fill(gpb_provider* p, int64_t r0, int64_t nl, const float* xt_dev, int m, float* out,
+               cudaStream_t st) {
+  if (nl <= 0 || m <= 0) return GPB_OK;
+  dim3 grid((unsigned)ceil_div(nl, 128), (unsigned)m);
+  cross_fill_kernel<<<grid, 128, 0, st>>>(p->X_d, r0, nl, p->d, xt_dev, p->dk, out);
+  GPB_CHECK_CUDA(cudaGetLastError());
+  return GPB_OK;
+}
 }  // namespace gpb
 
 extern "C" {

@@ -67,6 +67,9 @@ int provider_plan(gpb_provider* p);
 int provider_refresh_xs(gpb_provider* p);
 // Check and clear the device error word (synchronizes the stream).
 int provider_check_device_error(gpb_provider* p);
+// out[c][i] = k(x_{r0 + i}, x*_c) for i < nl, c < m (raw inputs; xt_dev [m][d] on the device).
+int cross_fill(gpb_provider* p, int64_t r0, int64_t nl, const float* xt_dev, int m, float* out,
+               cudaStream_t st);
 
 // out[c*out_ld + i] = scale * sum_j k(xrow_i, x_j) v[c*v_ld + j]  (+ noise * v for
 // the training rows when add_noise). `xrow_prescaled` holds nrow rows already

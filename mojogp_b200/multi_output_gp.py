@@ -122,6 +122,19 @@ class LMC:
                   float(tol), C.c_void_p(x.ctypes.data), C.byref(it))
         return x, it.value
 
+    def exact_variance(self, X_test: np.ndarray, max_cg: int = 100, tol: float = 1e-2,
+                       block_cols: int = 0):
+        """Exact posterior variance [m, T] of every task at X_test (observation
+        noise included); returns (variance, total CG iterations)."""
+        Xt = np.ascontiguousarray(X_test, np.float32)
+        m = Xt.shape[0]
+        var = np.zeros((m, self.T), np.float32)
+        it = C.c_int32()
+        _lib.call("gpb_lmc_predict_exact_variance", C.c_void_p(self.handle),
+                  C.c_void_p(Xt.ctypes.data), m, int(block_cols), int(max_cg), float(tol),
+                  C.c_void_p(var.ctypes.data), C.byref(it))
+        return var, it.value
+
     def destroy(self) -> None:
         if getattr(self, "handle", None):
             _lib.lib().gpb_lmc_destroy(C.c_void_p(self.handle))
@@ -319,10 +332,20 @@ class MultiOutputLMCGP:
     def log_marginal_likelihood(self) -> float:
         return -float(self.final_nll)
 
-    def predict(self, X_test, return_var: bool = False, return_std: bool = False):
-        """Mean [m, T]; with return_var / return_std also the LOVE variance / std [m, T]."""
+    def predict(self, X_test, return_var: bool = False, return_std: bool = False,
+                variance_method: str = "love"):
+        """Mean [m, T]; with return_var / return_std also the variance / std [m, T]
+        (observation noise included). variance_method (MultiOutputLMCGP.predict,
+        mojogp/multi_output_gp.py:5406-5556): 'love' sums per-latent LOVE
+        variances weighted by the row norms of A_s; 'exact' is the full LMC
+        posterior diagonal by batched CG (_predict_lmc_full_exact_variance_backend,
+        4360-4519, with CG iterations max(max_cg_iterations, 100) and tolerance
+        min(cg_tolerance, 1e-2)); 'mean_only' returns zero variance."""
         if self._lmc is None:
             raise RuntimeError("model must be fit first")
+        if variance_method not in ("love", "exact", "mean_only"):
+            raise ValueError("variance_method must be one of ('love', 'exact', 'mean_only'), "
+                             f"got '{variance_method}'")
         Xt = np.ascontiguousarray(X_test, np.float32)
         if Xt.ndim == 1:
             Xt = Xt[:, None]
@@ -335,6 +358,14 @@ class MultiOutputLMCGP:
         mean = (mean + self.mean_[None, :]).astype(np.float32)
         if not (return_var or return_std):
             return mean
+        if variance_method == "mean_only":
+            return mean, np.zeros_like(mean)
+        if variance_method == "exact":
+            tol = min(float(self.cg_tol), 1e-2) if self.cg_tol > 0 else 1e-2
+            var, _ = self._lmc.exact_variance(Xt, max(int(self.max_cg_iter), 100), tol)
+            if return_std:
+                return mean, np.sqrt(var)
+            return mean, var
         from .gp import _DEFAULT_PREDICT_LANCZOS_RANK
         from .prediction import PredictionCache
         avg_noise = float(np.mean(self.noise))

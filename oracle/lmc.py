@@ -35,6 +35,27 @@ def full_operator(specs, params_list, X, A, noise):
     return K, Ks, Gs
 
 
+def exact_variance(specs, params_list, X, Xtest, A, noise):
+    """Exact LMC posterior variance [m, T] (_predict_lmc_full_exact_variance_backend,
+    mojogp/multi_output_gp.py:4360-4519): for test point c and task t,
+    max(sum_s A_s[t, t] k_s(x*, x*) - r^T K_full^{-1} r + noise_t, 1e-10) with
+    r = sum_s A_s[:, t] (x) k_s(X, x*_c), by a dense float64 solve."""
+    K, _, _ = full_operator(specs, params_list, X, A, noise)
+    m, T = Xtest.shape[0], A.shape[1]
+    R = len(specs)
+    prior = np.zeros((m, T))
+    Rhs = np.zeros((K.shape[0], m * T))
+    for s, (spec, p) in enumerate(zip(specs, params_list)):
+        Kc = ok.kernel_matrix(spec, p, X, Xtest)  # [n, m]
+        kd = np.array([ok.kernel_matrix(spec, p, Xtest[c:c + 1])[0, 0] for c in range(m)])
+        prior += kd[:, None] * np.diag(A[s])[None, :]
+        for t in range(T):
+            Rhs[:, t::T] += np.kron(A[s][:, t:t + 1], Kc)
+    Sol = np.linalg.solve(K, Rhs)
+    corr = np.einsum("ij,ij->j", Rhs, Sol).reshape(m, T)
+    return np.maximum(prior - corr + np.asarray(noise)[None, :], 1e-10)
+
+
 class LmcPrecond:
     """P = sum_s (C_s (x) L_s)(C_s (x) L_s)^T + D; Woodbury apply, log|P|, N(0, P) probes."""
 

@@ -72,6 +72,9 @@ def main(out_path):
         res[tag] = {"nll": r["nll"], "gA": r["gA"].tolist(), "gnoise": r["gnoise"].tolist(),
                     "kgrads": r["kgrads"].tolist(), "alpha": r["alpha"][::37].tolist(),
                     "cg": r["cg_iters"]}
+        # Exact LMC variance through the sharded operator (every rank gets all).
+        ev, _ = lmc.exact_variance(Xl[:25] + 0.03, 300, 1e-5)
+        res[tag]["exact_var"] = ev.ravel().tolist()
     comm.barrier()
     if rank == 0:
         Path(out_path).write_text(json.dumps(res))

@@ -175,3 +175,51 @@ def test_lmc_bbmm_rbf16_tensor_core_gradients(gpb_lib):
     for key in ("kgrads", "gA", "gnoise"):
         np.testing.assert_allclose(got[key], ref[key], rtol=0,
                                    atol=1e-3 * np.abs(ref[key]).max(), err_msg=key)
+
+
+def _exact_var_ref(ks, ps, X, Xt, A, noise):
+    return olmc.exact_variance([k.to_spec(X.shape[1]) for k in ks], ps, X.astype(np.float64),
+                               Xt.astype(np.float64), A.astype(np.float64),
+                               noise.astype(np.float64))
+
+
+@pytest.mark.parametrize("block_cols", [0, 12])
+def test_lmc_exact_variance_vs_oracle(gpb_lib, block_cols):
+    X, ks, ps, A, noise, provs, lmc = _setup()
+    Xt = np.random.default_rng(6).uniform(-1.2, 1.2, size=(37, X.shape[1])).astype(np.float32)
+    # block_cols 12 at T = 3: blocks of 4 test points, the last one ragged (37 = 9 x 4 + 1).
+    var, iters = lmc.exact_variance(Xt, 300, 1e-6, block_cols)
+    ref = _exact_var_ref(ks, ps, X, Xt, A, noise)
+    assert var.shape == (37, 3) and iters > 0
+    np.testing.assert_allclose(var, ref, rtol=1e-3, atol=1e-5)
+    # Posterior variance lies between the noise floor and the prior + noise.
+    assert np.all(var >= noise[None, :] * (1 - 1e-4))
+
+
+def test_lmc_exact_variance_preconditioned(gpb_lib):
+    X, ks, ps, A, noise, provs, lmc = _ill_conditioned()
+    Xt = np.random.default_rng(7).uniform(-1, 1, size=(20, X.shape[1])).astype(np.float32)
+    ref = _exact_var_ref(ks, ps, X, Xt, A, noise)
+    plain, it_plain = lmc.exact_variance(Xt, 1000, 1e-5)
+    lmc.build_precond(15)
+    pc, it_pc = lmc.exact_variance(Xt, 1000, 1e-5)
+    assert it_pc < it_plain
+    for v in (plain, pc):
+        np.testing.assert_allclose(v, ref, rtol=2e-3, atol=2e-4)
+
+
+def test_lmc_gp_predict_variance_methods(gpb_lib):
+    X, Y = synthetic.config4(n=400)
+    gp = MultiOutputLMCGP(kernels=[RBF(), Matern32()], num_probes=8, cg_tolerance=1e-4)
+    gp.fit(X, Y, max_iterations=3, learning_rate=0.05)
+    Xt = X[:30] + 0.05
+    mean, var = gp.predict(Xt, return_var=True, variance_method="exact")
+    _, std = gp.predict(Xt, return_std=True, variance_method="exact")
+    np.testing.assert_allclose(std, np.sqrt(var), rtol=1e-5)
+    ref = _exact_var_ref(gp.kernels_resolved, gp.params_, X, Xt, gp.A, gp.noise)
+    np.testing.assert_allclose(var, ref, rtol=2e-3, atol=1e-4)
+    m0, v0 = gp.predict(Xt, return_var=True, variance_method="mean_only")
+    np.testing.assert_allclose(m0, mean)
+    assert not v0.any()
+    with pytest.raises(ValueError):
+        gp.predict(Xt, return_var=True, variance_method="bogus")

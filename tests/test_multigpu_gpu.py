@@ -61,7 +61,7 @@ def test_two_gpu_sharded_engine_matches_one_gpu(gpb_lib, tmp_path):
             bad.append(f"{tag} cg {a['cg']} vs {b['cg']}")
         if abs(a["nll"] - b["nll"]) >= 1e-4 * abs(a["nll"]):
             bad.append(f"{tag} nll {a['nll']} vs {b['nll']}")
-        for key in ("gA", "gnoise", "kgrads", "alpha"):
+        for key in ("gA", "gnoise", "kgrads", "alpha", "exact_var"):
             ref, got = np.asarray(a[key]), np.asarray(b[key])
             err = np.abs(got - ref).max() / max(np.abs(ref).max(), 1e-30)
             if err >= 1e-3:
