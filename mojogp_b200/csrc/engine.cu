@@ -116,7 +116,7 @@ int Engine::matvec(float* v_local, int64_t v_ld, int t, float* out, int64_t out_
   const int ntiles = (int)(rows_total / kJT);
   for (int c0 = 0; c0 < t; c0 += 16) {
     const int rem = t - c0;
-    const int T = kv_pick_t(rem);
+    const int T = kv_chunk_t(p->eval, p->DP, rem, p->gram_ok);
     const int tcols = std::min(rem, T);
     const int layout = kv_layout(p->eval, p->DP, T, p->gram_ok);
     const int W = kv_packed_width(p->eval, p->DP, T, p->gram_ok);

@@ -186,6 +186,8 @@ int k_pack(const float* xs, int DP, float* v, int64_t v_ld, int c0, int tcols, i
     return launch_pack_tc(xs, DP, v, v_ld, c0, tcols, nl, nl_pad, dst, upd_z, upd_beta, st);
   if (layout == KV_GRAM)
     return launch_pack_gram(xs, DP, v, v_ld, c0, tcols, nl, nl_pad, dst, upd_z, upd_beta, st);
+  if (layout == KV_GRAM1)
+    return launch_pack_gram1(xs, DP, T, v, v_ld, c0, tcols, nl, nl_pad, dst, upd_z, upd_beta, st);
   const bool dup = layout == KV_X2;
   pack_rows_kernel<<<(unsigned)ceil_div(nl_pad, 256), 256, 0, st>>>(
       xs, DP, v, v_ld, c0, tcols, dup ? 2 * (DP + T) : packed_width(DP, T), nl, nl_pad, dst, upd_z,

@@ -63,16 +63,20 @@ inline int kv_pick_t(int64_t remaining) {
 //             Matérn-3/2, Matérn-5/2 or RQ, T = 16, DP 8 or 16, and only when
 //             the caller vouches for bounded input norms (gram_ok);
 //             GPB_KV_GRAM=0 in the environment selects KV_TC instead;
+//   KV_GRAM1  the Gram kernel's MMA1 with an fp32 CUDA-core contraction
+//             (kv_tile_gram1_kernel) for T = 1, 4 or 8 under the same
+//             conditions; GPB_KV_GRAM1=0 pads those chunks to T = 16 instead;
 //   KV_TC     tensor-core contraction (kv_tiles_tc.cuh): fast leaves, T = 16,
 //             DP a multiple of 4 (default; GPB_KV_TC=0 in the environment
 //             selects KV_X2 instead);
 //   KV_X2     paired-row FFMA2 kernel (kv_tiles_x2.cuh): fast leaves, even DP,
 //             T >= 4; GPB_KV_SCALAR=1 disables it (and the TC kernel);
 //   KV_SCALAR everything else (and the composite-tree evaluator).
-enum KvLayout { KV_SCALAR = 0, KV_X2 = 1, KV_TC = 2, KV_GRAM = 3 };
+enum KvLayout { KV_SCALAR = 0, KV_X2 = 1, KV_TC = 2, KV_GRAM = 3, KV_GRAM1 = 4 };
 bool kv_x2_disabled();
 bool kv_tc_disabled();
 bool kv_gram_disabled();
+bool kv_gram1_disabled();
 // Largest max_i |x'_i|^2 (prescaled inputs) for which the Gram expansion keeps
 // the matvec within the 1e-5 relative bar (3xTF32 cross term, fp32 norms).
 constexpr float kGramMaxSqNorm = 100.f;
@@ -82,12 +86,25 @@ constexpr bool gram_leaf(int eval) {
 }
 inline int kv_layout(int eval, int DP, int T, bool gram_ok = false) {
   if (eval == kEvalGeneric || kv_x2_disabled()) return KV_SCALAR;
-  if (gram_ok && gram_leaf(eval) && T == 16 && (DP == 8 || DP == 16) && !kv_tc_disabled() &&
-      !kv_gram_disabled())
-    return KV_GRAM;
+  if (gram_ok && gram_leaf(eval) && (DP == 8 || DP == 16) && !kv_tc_disabled() &&
+      !kv_gram_disabled()) {
+    if (T == 16) return KV_GRAM;
+    if ((T == 1 || T == 4 || T == 8) && !kv_gram1_disabled()) return KV_GRAM1;
+  }
   if (T == 16 && DP % 4 == 0 && DP <= 32 && !kv_tc_disabled()) return KV_TC;
   if (DP % 2 == 0 && T >= 4) return KV_X2;
   return KV_SCALAR;
+}
+// Column-chunk width for `remaining` columns. On the Gram path a narrow chunk
+// runs on KV_GRAM1, or, when that is disabled, at T = 16 with zero-padded
+// columns (the Gram kernel's cost is the per-entry kernel evaluation, nearly
+// independent of T).
+inline int kv_chunk_t(int eval, int DP, int64_t remaining, bool gram_ok) {
+  const int t = kv_pick_t(remaining);
+  if (t < 16 && kv_layout(eval, DP, t, gram_ok) != KV_GRAM1 &&
+      kv_layout(eval, DP, 16, gram_ok) == KV_GRAM)
+    return 16;
+  return t;
 }
 inline bool kv_uses_x2(int eval, int DP, int T) { return kv_layout(eval, DP, T) == KV_X2; }
 // Floats per packed column row for this launch shape (the TC layout is
@@ -95,6 +112,7 @@ inline bool kv_uses_x2(int eval, int DP, int T) { return kv_layout(eval, DP, T) 
 inline int kv_packed_width(int eval, int DP, int T, bool gram_ok = false) {
   switch (kv_layout(eval, DP, T, gram_ok)) {
     case KV_GRAM: return 2 * DP + 8 + 32;
+    case KV_GRAM1: return 2 * DP + 8 + T;
     case KV_TC: return DP + 32;
     case KV_X2: return 2 * (DP + T);
     default: return ((DP + T) + 3) / 4 * 4;

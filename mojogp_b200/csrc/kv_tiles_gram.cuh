@@ -370,4 +370,217 @@ __global__ void __launch_bounds__(kGThreads, 1) kv_tile_gram_kernel(
   if (warp == kTmaWarp) tmem_dealloc(tmem, kGTmemCols);
 }
 
+// ---------------------------------------------------------------------------
+// Narrow Gram kernel: the same MMA1 (u on the tensor core, A from TMEM), but
+// the contraction with NV <= 8 columns runs on the CUDA cores in fp32
+// (acc_c += k_ij v_jc): below ~12 columns, NV FFMAs per entry cost less than
+// the hi / lo split, the TMEM store and the three MMA2 products, so a
+// 1-column Lanczos step or alpha solve runs near the MUFU bound instead of
+// paying for 16 columns.
+// CTA: 4 row tiles of 128 rows, 16 epilogue warps; per row tile two MMA1
+// issuer warps (even / odd chunks); one TMA warp. TMEM: [x hi | x lo] and the
+// norm k-step per row tile, then 5 stages x 16 columns of u per row tile.
+// Packed tile (floats): [B hi : 128 x (DP + 8)][B lo : 128 x DP][V : 128 x NV].
+constexpr int kG1RowTiles = 4;
+constexpr int kG1UStages = 5;
+constexpr int kG1Par = 2;
+constexpr int kG1Stages = 6;
+constexpr int kG1EpiThreads = 128 * kG1RowTiles;
+constexpr int kG1IssuerWarps = kG1Par * kG1RowTiles;
+constexpr int kG1Threads = kG1EpiThreads + 32 * kG1IssuerWarps + 32;
+constexpr uint32_t kG1ColX = 0;
+constexpr uint32_t kG1ColN = 32 * kG1RowTiles;
+constexpr uint32_t kG1ColS = kG1ColN + 8 * kG1RowTiles;
+static_assert(kG1ColS + 16 * kG1UStages * kG1RowTiles <= kGTmemCols, "TMEM budget");
+__host__ __device__ constexpr int gram1_tile_floats(int DP, int NV) {
+  return 128 * (2 * DP + 8) + 128 * NV;
+}
+
+template <int DP, int LEAF, int NV>
+__global__ void __launch_bounds__(kG1Threads, 1) kv_tile_gram1_kernel(
+    const float* __restrict__ xrow, int64_t nrow, const float* __restrict__ xv, int ntiles_total,
+    int tiles_per_split, const __grid_constant__ FastParams fp, TileEpilogue ep, int* err) {
+  static_assert(DP % 8 == 0 && DP <= 16, "K = DP in 8-wide tf32 k-steps, x hi / lo in 32 columns");
+  static_assert(NV == 1 || NV == 2 || NV == 4 || NV == 8, "narrow column counts");
+  constexpr int TILE = gram1_tile_floats(DP, NV);
+  constexpr int kChunks = 128 / kGChunk;
+  constexpr int kIssuer0 = kG1EpiThreads / 32;
+  constexpr int kTmaWarp = kIssuer0 + kG1IssuerWarps;
+  constexpr int kVOff = 128 * (2 * DP + 8);
+  extern __shared__ __align__(1024) float smem[];
+  float* ring_buf = smem;
+  __shared__ __align__(8) uint64_t full_bar[kG1Stages];   // TMA landed
+  __shared__ __align__(8) uint64_t tile_bar[kG1Stages];   // every epilogue warp is done with the slot
+  __shared__ __align__(8) uint64_t d1_bar[kG1RowTiles][kG1UStages];  // MMA1 of a chunk done
+  __shared__ __align__(8) uint64_t uf_bar[kG1RowTiles][kG1UStages];  // u of a chunk read
+  __shared__ uint32_t tslot;
+
+  const int tid = threadIdx.x;
+  const int warp = tid >> 5, lane = tid & 31;
+  const int split = blockIdx.y;
+  const int t0 = split * tiles_per_split;
+  const int ntiles = max(0, min(ntiles_total, t0 + tiles_per_split) - t0);
+  const int G = ntiles * kChunks;
+  const uint32_t tile_bytes = TILE * sizeof(float);
+
+  if (tid == 0) {
+    for (int s = 0; s < kG1Stages; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&tile_bar[s], kG1EpiThreads / 32);
+    }
+    for (int r = 0; r < kG1RowTiles; ++r)
+      for (int s = 0; s < kG1UStages; ++s) {
+        mbar_init(&d1_bar[r][s], 1);
+        mbar_init(&uf_bar[r][s], 4);
+      }
+    fence_barrier_init();
+  }
+  if (warp == kTmaWarp) tmem_alloc(&tslot, kGTmemCols);
+  fence_proxy_async_smem();
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tslot;
+  const int rt = tid / 128;
+  const int64_t i = (int64_t)blockIdx.x * kG1EpiThreads + tid;
+  const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
+  if (tid < kG1EpiThreads) {
+    float x[DP];
+#pragma unroll
+    for (int k = 0; k < DP; ++k) x[k] = i < nrow ? xrow[i * DP + k] : 0.f;
+    const uint32_t a_row = tmem + lane_off + kG1ColX + rt * 32;
+#pragma unroll
+    for (int k8 = 0; k8 < DP; k8 += 8) {
+      uint32_t h[8], l[8];
+#pragma unroll
+      for (int k = 0; k < 8; ++k) {
+        const float hv = tf32_hi(x[k8 + k]);
+        h[k] = __float_as_uint(hv);
+        l[k] = __float_as_uint(x[k8 + k] - hv);
+      }
+      tmem_st8(a_row + k8, h);
+      tmem_st8(a_row + 16 + k8, l);
+    }
+    float e[8] = {0.f, 0.f, 0.f, 1.f, 1.f, 1.f, 0.f, 0.f};
+    gram_split3(gram_sqnorm(x, DP), e[0], e[1], e[2]);
+    uint32_t eb[8];
+#pragma unroll
+    for (int k = 0; k < 8; ++k) eb[k] = __float_as_uint(e[k]);
+    tmem_st8(tmem + lane_off + kG1ColN + rt * 8, eb);
+    tmem_wait_st();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  auto off = [](int floats) -> uint64_t { return (uint64_t)((floats * 4) >> 4); };
+  const uint32_t idesc = make_idesc_tf32(128, 16);
+
+  if (warp == kTmaWarp) {
+    if (lane == 0) {
+      bool ok = true;
+      for (int kt = 0; kt < ntiles && ok; ++kt) {
+        const int slot = kt % kG1Stages;
+        if (kt >= kG1Stages) ok = mbar_wait_bounded(&tile_bar[slot], ((kt - kG1Stages) / kG1Stages) & 1);
+        if (!ok) break;
+        mbar_arrive_expect_tx(&full_bar[slot], tile_bytes);
+        bulk_copy_g2s(ring_buf + slot * TILE, xv + (int64_t)(t0 + kt) * TILE, tile_bytes,
+                      &full_bar[slot]);
+      }
+      if (!ok) atomicExch(err, DEV_WAIT_TIMEOUT);
+    }
+    __syncwarp();
+  } else if (warp >= kIssuer0) {
+    const int r = (warp - kIssuer0) / kG1Par, par = (warp - kIssuer0) % kG1Par;
+    if (lane == 0) {
+      // MMA1 of chunk c into stage c % 5 of row tile r, once the epilogue has
+      // read the stage's previous chunk.
+      const uint64_t dring0 = make_smem_desc(ring_buf, 2048, 128);
+      const uint32_t ax = tmem + kG1ColX + r * 32, an = tmem + kG1ColN + r * 8;
+      bool ok = true;
+      int last = -1;
+      for (int c = par; c < G && ok; c += kG1Par) {
+        const int st = c % kG1UStages;
+        const int kt = c / kChunks, q = c % kChunks, slot = kt % kG1Stages;
+        if (c >= kG1UStages) {
+          ok = mbar_wait_bounded(&uf_bar[r][st], ((c - kG1UStages) / kG1UStages) & 1);
+          if (!ok) break;
+        }
+        if (q < kG1Par) {
+          ok = mbar_wait_bounded(&full_bar[slot], (kt / kG1Stages) & 1);
+          if (!ok) break;
+        }
+        tc_fence_after();
+        const uint64_t db = dring0 + off(slot * TILE + q * 64);
+        const uint32_t d = tmem + kG1ColS + (r * kG1UStages + st) * 16;
+#pragma unroll
+        for (int ks = 0; ks < DP / 8; ++ks) {
+          mma_tf32_tmem_a(d, ax + ks * 8, db + off(ks * 1024), idesc, ks > 0 ? 1u : 0u);
+          mma_tf32_tmem_a(d, ax + ks * 8, db + off(128 * gram_kaug(DP) + ks * 1024), idesc, 1u);
+          mma_tf32_tmem_a(d, ax + 16 + ks * 8, db + off(ks * 1024), idesc, 1u);
+        }
+        mma_tf32_tmem_a(d, an, db + off(DP / 8 * 1024), idesc, 1u);
+        mma_commit(&d1_bar[r][st]);
+        last = c;
+      }
+      if (!ok) atomicExch(err, DEV_WAIT_TIMEOUT);
+      // No MMA of this thread may still be in flight when TMEM is released.
+      if (last >= 0) (void)mbar_wait_bounded(&d1_bar[r][last % kG1UStages], (last / kG1UStages) & 1);
+    }
+    __syncwarp();
+  } else {
+    const uint32_t s_base = tmem + lane_off + kG1ColS + rt * kG1UStages * 16;
+    float acc[NV];
+#pragma unroll
+    for (int c = 0; c < NV; ++c) acc[c] = 0.f;
+    bool ok = true;
+    for (int g = 0; g < G && ok; ++g) {
+      const int st = g % kG1UStages;
+      const int kt = g / kChunks, q = g % kChunks, slot = kt % kG1Stages;
+      // V is read from shared memory by these threads: observe the TMA completion.
+      if (q == 0) ok = mbar_wait_bounded(&full_bar[slot], (kt / kG1Stages) & 1);
+      if (ok) ok = mbar_wait_bounded(&d1_bar[rt][st], (g / kG1UStages) & 1);
+      if (!ok) break;
+      tc_fence_after();
+      float u[16];
+      tmem_ld16(s_base + st * 16, u);  // includes tcgen05.wait::ld
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&uf_bar[rt][st]);
+      const float* vs = ring_buf + slot * TILE + kVOff + q * 16 * NV;
+#pragma unroll
+      for (int h = 0; h < 16; ++h) {
+        const float kv = FastEval<LEAF>::value(u[h], fp);
+#pragma unroll
+        for (int c = 0; c < NV; ++c) acc[c] = fmaf(kv, vs[h * NV + c], acc[c]);
+      }
+      if (q == kChunks - 1) {
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tile_bar[slot]);
+      }
+    }
+    if (!ok) {
+      atomicExch(err, DEV_WAIT_TIMEOUT);
+    } else if (i < nrow) {
+      const bool partial = gridDim.y > 1;
+#pragma unroll
+      for (int c = 0; c < NV; ++c) {
+        if (c >= ep.tcols) continue;
+        if (partial) {
+          ep.out[((int64_t)split * NV + c) * ep.out_ld + i] = acc[c];
+        } else {
+          float o = ep.scale * acc[c];
+          if (ep.noise_v) {
+            const float nz = ep.noise_vec ? ep.noise_vec[i] : ep.noise;
+            o = fmaf(nz, ep.noise_v[c * ep.noise_ld + i], o);
+          }
+          ep.out[c * ep.out_ld + i] = o;
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == kTmaWarp) tmem_dealloc(tmem, kGTmemCols);
+}
+
 }  // namespace gpb

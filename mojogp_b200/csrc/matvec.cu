@@ -225,6 +225,58 @@ __global__ void pack_gram_kernel(const float* __restrict__ xs, int DP, float* __
   }
 }
 
+// Narrow Gram tile packing: per 128 columns [B hi | B lo | V : 128 x NV fp32]
+// (kv_tile_gram1_kernel), B as above, with the same optional p = z + beta p update.
+__global__ void pack_gram1_kernel(const float* __restrict__ xs, int DP, int NV,
+                                  float* __restrict__ v, int64_t v_ld, int c0, int tcols, int64_t n,
+                                  int64_t npad, float* __restrict__ dst,
+                                  const float* __restrict__ upd_z,
+                                  const float* __restrict__ upd_beta) {
+  const int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (j >= npad) return;
+  float* base = dst + (j / 128) * gram1_tile_floats(DP, NV);
+  const int jt = (int)(j % 128);
+  const int KA = gram_kaug(DP);
+  float y[32];
+  for (int q = 0; q < DP; ++q) y[q] = (j < n) ? xs[j * DP + q] : 0.f;
+  for (int q = 0; q < DP; ++q) {
+    const float b = -2.f * y[q];
+    const float hi = tf32_hi(b);
+    base[gram_xoff(jt, q)] = hi;
+    base[128 * KA + gram_xoff(jt, q)] = b - hi;
+  }
+  float e[8] = {1.f, 1.f, 1.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  gram_split3(gram_sqnorm(y, DP), e[3], e[4], e[5]);
+  for (int q = 0; q < 8; ++q) base[gram_xoff(jt, DP + q)] = e[q];
+  float* vb = base + 128 * (2 * DP + 8) + jt * NV;
+  for (int c = 0; c < NV; ++c) {
+    float val = 0.f;
+    if (j < n && c < tcols) {
+      const int64_t off = (int64_t)(c0 + c) * v_ld + j;
+      val = v[off];
+      if (upd_beta) {
+        const float b = upd_beta[c0 + c];
+        const float zz = upd_z[off];
+        val = (b == 0.f || b != b || val != val) ? zz : fmaf(b, val, zz);
+        v[off] = val;
+      }
+    }
+    vb[c] = val;
+  }
+}
+
+int launch_pack_gram1(const float* xs, int DP, int NV, float* v, int64_t v_ld, int c0, int tcols,
+                      int64_t n, int64_t npad, float* xv, const float* upd_z,
+                      const float* upd_beta, cudaStream_t stream) {
+  if (npad == 0) return GPB_OK;
+  GPB_REQUIRE((DP == 8 || DP == 16) && (NV == 1 || NV == 2 || NV == 4 || NV == 8), GPB_ERR_INVALID,
+              "narrow Gram packing needs DP in {8,16}, NV in {1,2,4,8}");
+  pack_gram1_kernel<<<(unsigned)ceil_div(npad, 128), 128, 0, stream>>>(
+      xs, DP, NV, v, v_ld, c0, tcols, n, npad, xv, upd_z, upd_beta);
+  GPB_CHECK_CUDA(cudaGetLastError());
+  return GPB_OK;
+}
+
 int launch_pack_gram(const float* xs, int DP, float* v, int64_t v_ld, int c0, int tcols, int64_t n,
                      int64_t npad, float* xv, const float* upd_z, const float* upd_beta,
                      cudaStream_t stream) {
@@ -234,6 +286,15 @@ int launch_pack_gram(const float* xs, int DP, float* v, int64_t v_ld, int c0, in
                                                                      npad, xv, upd_z, upd_beta);
   GPB_CHECK_CUDA(cudaGetLastError());
   return GPB_OK;
+}
+
+bool kv_gram1_disabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("GPB_KV_GRAM1");
+    v = (e && e[0] == '0') ? 1 : 0;
+  }
+  return v == 1;
 }
 
 bool kv_gram_disabled() {
@@ -264,6 +325,9 @@ int launch_pack(const float* xs, int DP, const float* v, int64_t v_ld, int tcols
   if (layout == KV_GRAM)
     return launch_pack_gram(xs, DP, const_cast<float*>(v), v_ld, 0, tcols, n, npad, xv, nullptr,
                             nullptr, stream);
+  if (layout == KV_GRAM1)
+    return launch_pack_gram1(xs, DP, T, const_cast<float*>(v), v_ld, 0, tcols, n, npad, xv,
+                             nullptr, nullptr, stream);
   if (layout == KV_X2) {
     pack_dup_kernel<<<(unsigned)ceil_div(npad, 256), 256, 0, stream>>>(xs, DP, v, v_ld, tcols, T,
                                                                       n, npad, xv);

@@ -27,5 +27,9 @@ int launch_pack_tc(const float* xs, int DP, float* v, int64_t v_ld, int c0, int 
 int launch_pack_gram(const float* xs, int DP, float* v, int64_t v_ld, int c0, int tcols, int64_t n,
                      int64_t npad, float* xv, const float* upd_z, const float* upd_beta,
                      cudaStream_t stream);
+// Narrow Gram tile packing (KV_GRAM1, NV = T columns in fp32), same arguments.
+int launch_pack_gram1(const float* xs, int DP, int NV, float* v, int64_t v_ld, int c0, int tcols,
+                      int64_t n, int64_t npad, float* xv, const float* upd_z,
+                      const float* upd_beta, cudaStream_t stream);
 
 }  // namespace gpb

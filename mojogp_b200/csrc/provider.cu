@@ -233,6 +233,25 @@ int provider_refresh_xs(gpb_provider* p) {
   return GPB_OK;
 }
 
+// *ok = max_i |xs_i|^2 over nrow prescaled rows is within the Gram bound.
+static int rows_sqnorm_bounded(gpb_provider* p, const float* xs, int64_t nrow, cudaStream_t stream,
+                               bool* ok) {
+  *ok = false;
+  if (!p->sqnorm_d) GPB_CHECK_CUDA(cudaMalloc(&p->sqnorm_d, sizeof(unsigned)));
+  GPB_CHECK_CUDA(cudaMemsetAsync(p->sqnorm_d, 0, sizeof(unsigned), stream));
+  max_sqnorm_kernel<<<(unsigned)ceil_div(nrow, 256), 256, 0, stream>>>(xs, nrow, p->DP,
+                                                                      p->sqnorm_d);
+  GPB_CHECK_CUDA(cudaGetLastError());
+  unsigned h = 0;
+  GPB_CHECK_CUDA(cudaMemcpyAsync(&h, p->sqnorm_d, sizeof(unsigned), cudaMemcpyDeviceToHost, stream));
+  GPB_CHECK_CUDA(cudaStreamSynchronize(stream));
+  float hf = 0.f;
+  std::memcpy(&hf, &h, sizeof(hf));
+  *ok = h != 0xFFFFFFFFu && hf <= kGramMaxSqNorm;
+  p->launches += 1;
+  return GPB_OK;
+}
+
 int provider_prescale_rows(gpb_provider* p, const float* x_raw, int64_t nrow, int slot,
                            const float** out, cudaStream_t stream) {
   void* buf = nullptr;
@@ -259,13 +278,16 @@ int provider_kv(gpb_provider* p, const float* xrow, int64_t nrow, const float* v
                 cudaStream_t stream) {
   if (nrow == 0 || ncols == 0) return GPB_OK;
   GPB_TRY(provider_refresh_xs(p));
-  // The Gram path's norm bound was checked for the training rows only.
-  const bool gram = p->gram_ok && xrow >= p->Xs_d && xrow < p->Xs_d + std::max<int64_t>(p->n, 1) * p->DP;
+  // The Gram path needs bounded prescaled norms on both sides: the training
+  // rows were checked when Xs was built; other rows (test points) are checked here.
+  bool gram = p->gram_ok;
+  if (gram && !(xrow >= p->Xs_d && xrow < p->Xs_d + std::max<int64_t>(p->n, 1) * p->DP))
+    GPB_TRY(rows_sqnorm_bounded(p, xrow, nrow, stream, &gram));
   const int64_t npad = round_up(std::max<int64_t>(p->n, 1), kJT);
   const int ntiles = (int)(npad / kJT);
   for (int64_t c0 = 0; c0 < ncols; c0 += 16) {
     const int64_t rem = ncols - c0;
-    const int T = kv_pick_t(rem);
+    const int T = kv_chunk_t(p->eval, p->DP, rem, gram);
     const int tcols = (int)std::min<int64_t>(rem, T);
     const int W = kv_packed_width(p->eval, p->DP, T, gram);
     void* xv = nullptr;
@@ -559,7 +581,8 @@ int gpb_matvec_layout(gpb_provider* p, int64_t ncols, int32_t* layout) {
   GPB_REQUIRE(p && layout && ncols > 0, GPB_ERR_INVALID, "bad arguments");
   GPB_CHECK_CUDA(cudaSetDevice(p->device));
   GPB_TRY(provider_refresh_xs(p));
-  *layout = kv_layout(p->eval, p->DP, kv_pick_t(ncols), p->gram_ok);
+  const int T = kv_chunk_t(p->eval, p->DP, ncols, p->gram_ok);
+  *layout = kv_layout(p->eval, p->DP, T, p->gram_ok);
   return GPB_OK;
 }
 

@@ -85,8 +85,9 @@ def test_gram_param_update_rechecks_bound(gpb_lib):
 
 
 def test_gram_rows_and_cross(gpb_lib):
-    # Row-sharded output rows use the Gram path; the cross matvec (test rows
-    # with unchecked norms) uses the difference form. Both against the oracle.
+    # Row-sharded output rows use the Gram path; the cross matvec checks the
+    # test rows' norms and takes the Gram path when they are bounded, the
+    # difference form otherwise (shifted rows below). All against the oracle.
     k, p, X, V = _setup("rbf_ard", 2600, 16, 16, seed=4)
     prov = Provider(X, k, p, 0.1)
     full = prov.matvec_host(V)
@@ -100,6 +101,25 @@ def test_gram_rows_and_cross(gpb_lib):
     got = prov.cross_matvec_host(Xt, V)
     ref = ok.cross_matvec(k.to_spec(16), p, Xt, X, V)
     assert rel_fro(got, ref) < 1e-5
+    Xf = (Xt + 6.0).astype(np.float32)  # far outside the norm bound
+    assert rel_fro(prov.cross_matvec_host(Xf, V), ok.cross_matvec(k.to_spec(16), p, Xf, X, V)) < 1e-5
+
+
+@pytest.mark.parametrize("t", [1, 3, 8, 19])
+@pytest.mark.parametrize("kname", ["rbf_ard", "m52_ard"])
+def test_gram_narrow_blocks(gpb_lib, kname, t):
+    # Fewer than 16 columns (a Lanczos step, the alpha solve) run on the narrow
+    # Gram kernel (1, 4 or 8 columns); a 19-column block is one 16-column
+    # chunk on the Gram kernel plus a 3-column narrow chunk.
+    ell = (0.5, 3.0) if kname.startswith("rbf") else (1.5, 3.0)
+    d = 16 if t in (3, 19) else 8
+    k, p, X, V = _setup(kname, 2300, d, t, seed=30 + t, ell=ell)
+    prov = Provider(X, k, p, 0.1)
+    assert prov.matvec_layout(t) == ("gram-narrow" if t <= 8 else "gram-tensor-core")
+    ref = ok.forward_matvec(k.to_spec(d), p, X, V, noise=0.1)
+    assert rel_fro(prov.matvec_host(V), ref) < 1e-5
+    Xt = np.random.default_rng(t).standard_normal((101, d)).astype(np.float32)
+    assert rel_fro(prov.cross_matvec_host(Xt, V), ok.cross_matvec(k.to_spec(d), p, Xt, X, V)) < 1e-5
 
 
 @pytest.mark.parametrize("kname,n,d,t", [("rbf_ard", 3000, 16, 16), ("rbf_iso", 1000, 8, 11),
