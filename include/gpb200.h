@@ -370,7 +370,7 @@ int gpb_tc_selftest(int32_t device, int32_t variant, const float* a_host, const 
  * counterpart; diagnostics and tests): 0 scalar FFMA, 1 paired-row FFMA2,
  * 2 tensor-core contraction, 3 Gram form (both contractions on the tensor
  * core, chosen only for bounded prescaled input norms), 4 narrow Gram form
- * (tensor-core distances, fp32 CUDA-core contraction; 1, 4 or 8 columns). */
+ * (tensor-core distances, fp32 CUDA-core contraction; 1-column chunks). */
 int gpb_matvec_layout(gpb_provider* p, int64_t ncols, int32_t* layout);
 
 /* Same result as gpb_forward_matvec, but the call allocates no device memory:

@@ -170,7 +170,7 @@ int kv_launch_gram1(const KvLaunch& L) {
 
 template <int DP, int T, class Ev>
 int kv_launch_one(const KvLaunch& L) {
-  if constexpr (!Ev::kGeneric && (T == 1 || T == 4 || T == 8) && (DP == 8 || DP == 16)) {
+  if constexpr (!Ev::kGeneric && T == 1 && (DP == 8 || DP == 16)) {
     if constexpr (gram_leaf(Ev::kLeaf)) {
       if (kv_layout(L.eval, DP, T, L.gram_ok) == KV_GRAM1)
         return kv_launch_gram1<DP, Ev::kLeaf, T>(L);

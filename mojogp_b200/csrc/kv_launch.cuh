@@ -64,8 +64,11 @@ inline int kv_pick_t(int64_t remaining) {
 //             the caller vouches for bounded input norms (gram_ok);
 //             GPB_KV_GRAM=0 in the environment selects KV_TC instead;
 //   KV_GRAM1  the Gram kernel's MMA1 with an fp32 CUDA-core contraction
-//             (kv_tile_gram1_kernel) for T = 1, 4 or 8 under the same
-//             conditions; GPB_KV_GRAM1=0 pads those chunks to T = 16 instead;
+//             (kv_tile_gram1_kernel) for T = 1 under the same conditions
+//             (measured at n = 3e5: 3.2e12 entries/s against 2.35e12 for the
+//             Gram kernel; at 4 and 8 columns the Gram kernel with padded
+//             columns is as fast or faster, so those chunks run at T = 16);
+//             GPB_KV_GRAM1=0 pads 1-column chunks to T = 16 as well;
 //   KV_TC     tensor-core contraction (kv_tiles_tc.cuh): fast leaves, T = 16,
 //             DP a multiple of 4 (default; GPB_KV_TC=0 in the environment
 //             selects KV_X2 instead);
@@ -89,7 +92,7 @@ inline int kv_layout(int eval, int DP, int T, bool gram_ok = false) {
   if (gram_ok && gram_leaf(eval) && (DP == 8 || DP == 16) && !kv_tc_disabled() &&
       !kv_gram_disabled()) {
     if (T == 16) return KV_GRAM;
-    if ((T == 1 || T == 4 || T == 8) && !kv_gram1_disabled()) return KV_GRAM1;
+    if (T == 1 && !kv_gram1_disabled()) return KV_GRAM1;
   }
   if (T == 16 && DP % 4 == 0 && DP <= 32 && !kv_tc_disabled()) return KV_TC;
   if (DP % 2 == 0 && T >= 4) return KV_X2;

@@ -373,10 +373,10 @@ __global__ void __launch_bounds__(kGThreads, 1) kv_tile_gram_kernel(
 // ---------------------------------------------------------------------------
 // Narrow Gram kernel: the same MMA1 (u on the tensor core, A from TMEM), but
 // the contraction with NV <= 8 columns runs on the CUDA cores in fp32
-// (acc_c += k_ij v_jc): below ~12 columns, NV FFMAs per entry cost less than
-// the hi / lo split, the TMEM store and the three MMA2 products, so a
-// 1-column Lanczos step or alpha solve runs near the MUFU bound instead of
-// paying for 16 columns.
+// (acc_c += k_ij v_jc) instead of the hi / lo split, the TMEM store and the
+// three MMA2 products. The host routes only 1-column chunks here (a Lanczos
+// step, an alpha solve): those run at 75 % of the MUFU bound, 1.37x the Gram
+// kernel's entry rate; at 4 and 8 columns the Gram kernel is as fast or faster.
 // CTA: 4 row tiles of 128 rows, 16 epilogue warps; per row tile two MMA1
 // issuer warps (even / odd chunks); one TMA warp. TMEM: [x hi | x lo] and the
 // norm k-step per row tile, then 5 stages x 16 columns of u per row tile.

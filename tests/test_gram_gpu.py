@@ -105,17 +105,17 @@ def test_gram_rows_and_cross(gpb_lib):
     assert rel_fro(prov.cross_matvec_host(Xf, V), ok.cross_matvec(k.to_spec(16), p, Xf, X, V)) < 1e-5
 
 
-@pytest.mark.parametrize("t", [1, 3, 8, 19])
+@pytest.mark.parametrize("t", [1, 3, 8, 17])
 @pytest.mark.parametrize("kname", ["rbf_ard", "m52_ard"])
 def test_gram_narrow_blocks(gpb_lib, kname, t):
-    # Fewer than 16 columns (a Lanczos step, the alpha solve) run on the narrow
-    # Gram kernel (1, 4 or 8 columns); a 19-column block is one 16-column
-    # chunk on the Gram kernel plus a 3-column narrow chunk.
+    # A single column (a Lanczos step, the alpha solve) runs on the narrow Gram
+    # kernel; 2-15 columns on the Gram kernel with zero-padded columns; a
+    # 17-column block is a 16-column chunk plus a 1-column narrow chunk.
     ell = (0.5, 3.0) if kname.startswith("rbf") else (1.5, 3.0)
-    d = 16 if t in (3, 19) else 8
+    d = 16 if t in (3, 17) else 8
     k, p, X, V = _setup(kname, 2300, d, t, seed=30 + t, ell=ell)
     prov = Provider(X, k, p, 0.1)
-    assert prov.matvec_layout(t) == ("gram-narrow" if t <= 8 else "gram-tensor-core")
+    assert prov.matvec_layout(t) == ("gram-narrow" if t == 1 else "gram-tensor-core")
     ref = ok.forward_matvec(k.to_spec(d), p, X, V, noise=0.1)
     assert rel_fro(prov.matvec_host(V), ref) < 1e-5
     Xt = np.random.default_rng(t).standard_normal((101, d)).astype(np.float32)
