@@ -49,8 +49,11 @@ def parse():
     ap.add_argument("--rhs", dest="t", type=int, default=16)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
-    ap.add_argument("--workload", default="c3", choices=["c3", "c5"],
-                    help="c3: the headline K·V / fit line (default); c5: LOVE prediction at scale")
+    ap.add_argument("--workload", default="c3", choices=["c1", "c2", "c3", "c4", "c5"],
+                    help="c3: the headline K·V / fit line (default); c1, c2, c4: the other "
+                         "fit configurations (1 GPU); c5: LOVE prediction at scale")
+    ap.add_argument("--cfg-iters", type=int, default=50,
+                    help="c1 / c2 / c4: outer fit iterations")
     ap.add_argument("--test-rows", type=int, default=0,
                     help="c5: test points (default = --rows)")
     ap.add_argument("--love-rank", type=int, default=256)
@@ -216,6 +219,92 @@ def run_love(args, rank: int, world: int, local: int) -> None:
         comm.close()
 
 
+def run_config(args, rank: int, world: int, local: int) -> None:
+    """Configs 1, 2 and 4 through the public model API on one GPU: a full fit
+    (fit s/iter = median per-iteration time; the LMC fit, which records no
+    per-iteration times, is total / iterations) and, for config 1, the LOVE
+    prediction of 128 test points. Config 1 also times the reference's NumPy
+    exact-Cholesky fit iteration on the host cores as its CPU baseline."""
+    if rank != 0:
+        return
+    from mojogp_b200 import synthetic
+    from mojogp_b200.gp import SingleOutputGP
+    from mojogp_b200.kernel import RBF, Matern32, Matern52
+    from mojogp_b200.multi_output_gp import MultiOutputLMCGP
+    wl, iters = args.workload, args.cfg_iters
+    sampler = ClockSampler(local)
+    extra = {}
+    if wl in ("c1", "c2"):
+        if wl == "c1":
+            X, y, Xs = synthetic.config1()
+            make = lambda: SingleOutputGP(RBF(), device=local)
+            kw = dict(method="matrix_free")
+            cfg = {"workload": "config1 RBF 1-D fit + LOVE predict", "n": 2000, "d": 1,
+                   "t": 11, "n_test": 128}
+        else:
+            X, y = synthetic.config2()
+            Xs = None
+            make = lambda: SingleOutputGP(Matern52(ard=True), device=local)
+            kw = dict(method="matrix_free", num_probes=15, preconditioner="greedy",
+                      preconditioner_rank=100)
+            cfg = {"workload": "config2 Matern-5/2 ARD fit, pivoted-Cholesky rank 100",
+                   "n": X.shape[0], "d": X.shape[1], "t": 16}
+        make().fit(X, y, max_iterations=2, **kw)  # warm-up: kernel loads
+        gp = make()
+        sampler.start()
+        t0 = time.perf_counter()
+        res = gp.fit(X, y, max_iterations=iters, **kw)
+        fit_s = time.perf_counter() - t0
+        if Xs is not None:
+            t1 = time.perf_counter()
+            mean, std = gp.predict(Xs, return_std=True, variance_method="love")
+            extra["predict_s"] = time.perf_counter() - t1
+            extra["mean_std"] = float(np.mean(std))
+        clocks = sampler.stop()
+        it = np.asarray(res.iter_times_ms, np.float64)
+        s_iter = float(np.median(it[4:] if it.size > 5 else it)) / 1e3
+        extra.update({"final_nll": float(res.nll), "iterations": int(res.iterations),
+                      "cg_iters_median": float(np.median(res.cg_iterations_history))})
+    else:
+        X, Y = synthetic.config4()
+        make = lambda: MultiOutputLMCGP(kernels=[RBF(), Matern32(), RBF(ard=True)],
+                                        num_probes=15, device=local)
+        make().fit(X, Y, max_iterations=2, method="matrix_free")
+        gp = make()
+        sampler.start()
+        t0 = time.perf_counter()
+        gp.fit(X, Y, max_iterations=iters, method="matrix_free")
+        fit_s = time.perf_counter() - t0
+        clocks = sampler.stop()
+        done = len(gp.nll_history)
+        s_iter = fit_s / max(done, 1)
+        extra.update({"final_nll": float(gp.final_nll), "iterations": done,
+                      "cg_iters_median": float(np.median(gp.cg_iterations_history)),
+                      "cg_iters_max": int(np.max(gp.cg_iterations_history)),
+                      "precond_rebuilds": int(gp.precond_rebuild_count),
+                      "tile_kernels": [p.matvec_layout(16) for p in gp._lmc.providers]})
+        cfg = {"workload": "config4 LMC T=4, R=3 (RBF, Matern-3/2, RBF-ARD) fit",
+               "n": X.shape[0], "d": X.shape[1], "T": 4, "R": 3, "t": 16}
+    line = {
+        "metric": "fit s/iter", "value": s_iter, "unit": "s", "n_gpus": 1, "steps": iters,
+        "warmup": 2, "ms_per_step": s_iter * 1e3, "higher_is_better": False,
+        "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": f"synthetic ({wl} recipe)", "config": cfg, "fit_total_s": fit_s,
+        **extra, "clocks": clocks,
+    }
+    if wl == "c1" and not args.no_cpu_baseline:
+        from oracle import cpu_baseline
+        gpp = gp.get_params()
+        sec = cpu_baseline.time_exact_fit_iteration(
+            X, y - gpp["mean"], np.array([gpp["rbf_lengthscale"]]), gpp["rbf_outputscale"],
+            gpp["noise"], reps=3)
+        line["cpu_baseline"] = {"value": sec, "unit": "s", "cores": os.cpu_count() or 1,
+                                "kind": "port",
+                                "sample": "one exact-Cholesky fit iteration at n = 2000 (LML + "
+                                          "gradient, float64 NumPy + BLAS)"}
+    print(json.dumps(line, default=float), flush=True)
+
+
 def main():
     args = parse()
     rank = int(os.environ.get("RANK", "0"))
@@ -226,6 +315,9 @@ def main():
         return
     if args.workload == "c5":
         run_love(args, rank, world, local)
+        return
+    if args.workload in ("c1", "c2", "c4"):
+        run_config(args, rank, world, local)
         return
 
     from mojogp_b200 import _lib, synthetic

@@ -156,6 +156,9 @@ int provider_plan(gpb_provider* p) {
     const float c = std::sqrt(c2);
     p->eval = L.type;
     p->DP = kv_pick_dp(L.type, L.ndims);
+    // 3-8 input dims on a leaf the Gram tensor-core kernels take: pad to 8
+    // (zero dims change no distance) so that those kernels can run.
+    if (gram_leaf(L.type) && L.ndims >= 3 && L.ndims <= 8) p->DP = 8;
     ps.DP = p->DP;
     ps.nd = L.ndims;
     for (int q = 0; q < L.ndims; ++q) {

@@ -71,3 +71,41 @@ def time_matvec_sample(X, V, ell, os_, target_s: float = 15.0, threads: int | No
     pairs = nrows * n
     return {"seconds": dt, "rows": nrows, "pairs": pairs, "pairs_per_s": pairs / dt,
             "threads": threads}
+
+
+def exact_fit_iteration(X, y, ell, os_, noise):
+    """One fit iteration of the reference's NumPy exact-Cholesky route
+    (tests/integration/test_exactgp_variance_accuracy.py:30-46 and
+    tests/shared/dense_references.py:67-82 restated): RBF kernel matrix,
+    Cholesky of K + noise I, alpha, the log marginal likelihood per sample and
+    its gradient w.r.t. (lengthscales, outputscale, noise) through
+    0.5 tr((alpha alpha^T - K^-1) dK). Returns (nll, gradient)."""
+    Xs = np.asarray(X, np.float64) / np.asarray(ell, np.float64)
+    n = Xs.shape[0]
+    sq = (Xs * Xs).sum(1)
+    D = np.maximum(sq[:, None] + sq[None, :] - 2.0 * Xs @ Xs.T, 0.0)
+    E = np.exp(-0.5 * D)
+    K = os_ * E
+    Ky = K + noise * np.eye(n)
+    L = np.linalg.cholesky(Ky)
+    alpha = np.linalg.solve(L.T, np.linalg.solve(L, np.asarray(y, np.float64)))
+    Kinv = np.linalg.solve(L.T, np.linalg.solve(L, np.eye(n)))
+    W = np.outer(alpha, alpha) - Kinv
+    nll = (0.5 * y @ alpha + np.log(np.diag(L)).sum() + 0.5 * n * np.log(2 * np.pi)) / n
+    grads = []
+    for k in range(Xs.shape[1]):
+        dk = Xs[:, k][:, None] - Xs[:, k][None, :]
+        grads.append(-0.5 * (W * (K * dk * dk / ell[k])).sum() / n)
+    grads.append(-0.5 * (W * E).sum() / n)
+    grads.append(-0.5 * np.trace(W) / n)
+    return float(nll), np.array(grads)
+
+
+def time_exact_fit_iteration(X, y, ell, os_, noise, reps: int = 3):
+    """Median seconds of exact_fit_iteration over `reps` runs (BLAS threads as set)."""
+    ts = []
+    for _ in range(reps):
+        t0 = time.perf_counter()
+        exact_fit_iteration(X, y, ell, os_, noise)
+        ts.append(time.perf_counter() - t0)
+    return float(np.median(ts))
