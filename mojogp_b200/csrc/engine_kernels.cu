@@ -198,12 +198,17 @@ int k_pack(const float* xs, int DP, float* v, int64_t v_ld, int c0, int tcols, i
 
 // ------------------------------------------------------------ reductions
 int Reducer::ensure(int max_blocks, int k) {
-  GPB_TRY(partial.ensure((size_t)max_blocks * k * sizeof(double)));
+  // Grow geometrically: callers whose k rises by one per step (Lanczos
+  // re-orthogonalisation against a growing basis) must not pay a device
+  // free + allocation, and the synchronisation that comes with it, every step.
+  const size_t need = (size_t)max_blocks * k * sizeof(double);
+  if (partial.bytes < need) GPB_TRY(partial.ensure(std::max(need, 2 * partial.bytes)));
+  const size_t need_s = (size_t)k * sizeof(double);
+  if (sums.bytes < need_s) GPB_TRY(sums.ensure(std::max(need_s, 2 * sums.bytes)));
   if (counter.bytes < sizeof(unsigned) * 4) {
     GPB_TRY(counter.ensure(sizeof(unsigned) * 4));
     GPB_CHECK_CUDA(cudaMemset(counter.ptr, 0, sizeof(unsigned) * 4));
   }
-  GPB_TRY(sums.ensure((size_t)k * sizeof(double)));
   return GPB_OK;
 }
 
