@@ -103,3 +103,63 @@ def test_sharded_cg_step_matches_unsharded():
     for _, pap, full in res:
         np.testing.assert_allclose(pap, np.sum(Pm * Ap, axis=0), rtol=1e-12)
         np.testing.assert_allclose(full, Ap, rtol=1e-12)
+
+
+class _GlooComm:
+    """Stand-in for distributed.Communicator's host reductions over gloo (test-only)."""
+
+    def __init__(self, rank, world):
+        self.rank, self.world = rank, world
+
+    def allreduce_sum(self, buf):
+        import torch
+        import torch.distributed as dist
+        t = torch.from_numpy(np.ascontiguousarray(buf, np.float64).copy())
+        dist.all_reduce(t)
+        return t.numpy()
+
+
+class _RowwiseCache:
+    """Stand-in for a prediction cache: mean / variance as fixed functions of each row."""
+
+    rank = 8
+
+    def predict(self, Xt, return_var=True):
+        m = np.sin(Xt).sum(1).astype(np.float32)
+        v = (1.0 + np.cos(Xt).sum(1) ** 2).astype(np.float32)
+        return m, (v if return_var else None)
+
+
+def _sharded_predict_worker(rank, world, port, m, q):
+    import torch.distributed as dist
+    from mojogp_b200.prediction import PredictionCache
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank,
+                            world_size=world)
+    Xt = np.random.default_rng(3).standard_normal((m, 3)).astype(np.float32)
+    mean, var = PredictionCache.predict_sharded(_RowwiseCache(), Xt, _GlooComm(rank, world))
+    q.put((rank, mean, var))
+    dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world,m", [(2, 101), (3, 2), (2, 0)])
+def test_sharded_prediction_assembles_every_row_on_every_rank(world, m):
+    """X* sharding (PredictionCache.predict_sharded): each rank predicts its slice
+    of the test rows, one all-reduce assembles all rows on every rank; ragged
+    and empty slices included (m < world, m = 0)."""
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_sharded_predict_worker, args=(r, world, port, m, q))
+             for r in range(world)]
+    for p in procs:
+        p.start()
+    res = [q.get(timeout=120) for _ in range(world)]
+    for p in procs:
+        p.join(30)
+        assert p.exitcode == 0
+    Xt = np.random.default_rng(3).standard_normal((m, 3)).astype(np.float32)
+    ref_m, ref_v = _RowwiseCache().predict(Xt)
+    for _, mean, var in res:
+        assert mean.shape == (m,) and var.shape == (m,)
+        np.testing.assert_array_equal(mean, ref_m)
+        np.testing.assert_array_equal(var, ref_v)
