@@ -123,6 +123,16 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
   }
 }
 
+// Before a producer's CTA may exit: wait (bounded) until every bulk copy it
+// issued into a ring of S slots has landed. Tile kt went to slot kt % S with
+// phase parity (kt / S) & 1, so the last S tiles cover every copy that can
+// still be in flight; on the normal path these phases completed long ago.
+template <int S>
+__device__ __forceinline__ void drain_ring(uint64_t* full_bar, int issued) {
+  for (int kt = issued > S ? issued - S : 0; kt < issued; ++kt)
+    (void)mbar_wait_bounded(&full_bar[kt % S], (uint32_t)((kt / S) & 1), 100000000ull);
+}
+
 // 1-D bulk copy global -> shared through the TMA engine, completing on `bar`.
 // dst, src 16-byte aligned; bytes a multiple of 16.
 __device__ __forceinline__ void bulk_copy_g2s(void* dst, const void* src, uint32_t bytes,

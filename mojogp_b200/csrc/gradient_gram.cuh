@@ -155,14 +155,17 @@ __global__ void __launch_bounds__(kGBThreads, 1) gb_kernel(
   if (warp == kTma) {
     if (lane == 0) {
       bool ok = true;
+      int issued = 0;
       for (int kt = 0; kt < ntiles && ok; ++kt) {
         const int slot = kt % kGBStages;
         if (kt >= kGBStages) ok = mbar_wait_bounded(&tile_bar[slot], ((kt - kGBStages) / kGBStages) & 1);
         if (!ok) break;
         mbar_arrive_expect_tx(&full_bar[slot], tile_bytes);
         bulk_copy_g2s(ring + slot * TILE, xv + (int64_t)(t0 + kt) * TILE, tile_bytes, &full_bar[slot]);
+        ++issued;
       }
       if (!ok) atomicExch(err, DEV_WAIT_TIMEOUT);
+      drain_ring<kGBStages>(full_bar, issued);
     }
     __syncwarp();
   } else if (warp >= kIss0) {

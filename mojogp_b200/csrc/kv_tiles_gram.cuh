@@ -204,6 +204,7 @@ __global__ void __launch_bounds__(kGThreads, 1) kv_tile_gram_kernel(
   if (warp == kTmaWarp) {
     if (lane == 0) {
       bool ok = true;
+      int issued = 0;
       for (int kt = 0; kt < ntiles && ok; ++kt) {
         const int slot = kt % kGStages;
         GRAM_T0(tw);
@@ -213,8 +214,10 @@ __global__ void __launch_bounds__(kGThreads, 1) kv_tile_gram_kernel(
         mbar_arrive_expect_tx(&full_bar[slot], tile_bytes);
         bulk_copy_g2s(ring_buf + slot * TILE, xv + (int64_t)(t0 + kt) * TILE, tile_bytes,
                       &full_bar[slot]);
+        ++issued;
       }
       if (!ok) atomicExch(err, DEV_WAIT_TIMEOUT);
+      drain_ring<kGStages>(full_bar, issued);
     }
     __syncwarp();
   } else if (warp >= kIssuer0) {
@@ -478,6 +481,7 @@ __global__ void __launch_bounds__(kG1Threads, 1) kv_tile_gram1_kernel(
   if (warp == kTmaWarp) {
     if (lane == 0) {
       bool ok = true;
+      int issued = 0;
       for (int kt = 0; kt < ntiles && ok; ++kt) {
         const int slot = kt % kG1Stages;
         if (kt >= kG1Stages) ok = mbar_wait_bounded(&tile_bar[slot], ((kt - kG1Stages) / kG1Stages) & 1);
@@ -485,8 +489,10 @@ __global__ void __launch_bounds__(kG1Threads, 1) kv_tile_gram1_kernel(
         mbar_arrive_expect_tx(&full_bar[slot], tile_bytes);
         bulk_copy_g2s(ring_buf + slot * TILE, xv + (int64_t)(t0 + kt) * TILE, tile_bytes,
                       &full_bar[slot]);
+        ++issued;
       }
       if (!ok) atomicExch(err, DEV_WAIT_TIMEOUT);
+      drain_ring<kG1Stages>(full_bar, issued);
     }
     __syncwarp();
   } else if (warp >= kIssuer0) {

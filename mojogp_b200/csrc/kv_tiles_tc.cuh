@@ -90,9 +90,11 @@ __global__ void __launch_bounds__(kTcThreads + 32, 2) kv_tile_tc_kernel(
 
   if (warp == 4) {
     if (lane == 0) {
+      int issued = 0;
       for (int s = 0; s < kTcStages && s < ntiles; ++s) {
         mbar_arrive_expect_tx(&full_bar[s], tile_bytes);
         bulk_copy_g2s(ring_buf + s * TILE, xv + (int64_t)(t0 + s) * TILE, tile_bytes, &full_bar[s]);
+        ++issued;
       }
       const uint32_t idesc = make_idesc_tf32(128, 16);
       int g = 0;
@@ -132,6 +134,7 @@ __global__ void __launch_bounds__(kTcThreads + 32, 2) kv_tile_tc_kernel(
             mbar_arrive_expect_tx(&full_bar[slot], tile_bytes);
             bulk_copy_g2s(ring_buf + slot * TILE, xv + (int64_t)(t0 + kt + kTcStages) * TILE,
                           tile_bytes, &full_bar[slot]);
+            ++issued;
           }
         }
       }
@@ -139,6 +142,7 @@ __global__ void __launch_bounds__(kTcThreads + 32, 2) kv_tile_tc_kernel(
         atomicExch(err, DEV_WAIT_TIMEOUT);
         atomicExch(&abort_flag, 1);
       }
+      drain_ring<kTcStages>(full_bar, issued);
     }
   } else {
     const int64_t row0 = (int64_t)blockIdx.x * (128 * kTcRows) + tid;
