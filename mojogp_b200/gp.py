@@ -33,6 +33,42 @@ _DEFAULT_PREDICT_MAX_CG_ITER = 300
 _DEFAULT_PREDICT_CG_TOL = 1e-3
 
 
+def _prediction_lanczos_rank(rank_hint: Optional[int], is_ard: bool) -> int:
+    """LOVE root rank: at least 100, at least 200 for ARD kernels
+    (_prediction_lanczos_rank, gp.py:112-138, continuous kernels)."""
+    rank = int(rank_hint) if rank_hint is not None else 0
+    floor = _DEFAULT_PREDICT_LANCZOS_RANK
+    if is_ard:
+        floor = max(floor, _DEFAULT_ARD_PREDICT_LANCZOS_RANK)
+    return max(rank, floor)
+
+
+def _prediction_solver_config(train_info: Optional[dict], rank_hint: Optional[int], *,
+                              is_ard: bool, max_cg_iterations: Optional[int] = None,
+                              cg_tolerance: Optional[float] = None,
+                              precond_rank: Optional[int] = None,
+                              max_root_decomposition_size: Optional[int] = None) -> dict:
+    """Prediction solver settings from the training settings and explicit
+    overrides (_prediction_solver_config, gp.py:141-199, continuous kernels):
+    CG iterations max(training, 300), tolerance min(training, 1e-3), the
+    training preconditioner rank (10 when unknown), the LOVE rank above."""
+    ti = train_info or {}
+    pr = int(precond_rank if precond_rank is not None else ti.get("precond_rank", 10))
+    rank = _prediction_lanczos_rank(rank_hint, is_ard)
+    if max_root_decomposition_size is not None:
+        rank = int(max_root_decomposition_size)
+    it = int(ti.get("max_cg_iterations", ti.get("max_cg_iter", _DEFAULT_PREDICT_MAX_CG_ITER)))
+    tol = float(ti.get("cg_tolerance", ti.get("cg_tol", _DEFAULT_PREDICT_CG_TOL)))
+    return {
+        "max_cg_iterations": int(max_cg_iterations if max_cg_iterations is not None
+                                 else max(it, _DEFAULT_PREDICT_MAX_CG_ITER)),
+        "cg_tolerance": float(cg_tolerance if cg_tolerance is not None
+                              else min(tol, _DEFAULT_PREDICT_CG_TOL)),
+        "precond_rank": pr,
+        "max_root_decomposition_size": rank,
+    }
+
+
 @dataclass
 class TrainingResult:
     params: np.ndarray
@@ -218,21 +254,15 @@ class SingleOutputGP:
 
     # ---------------------------------------------------------------- predict
     def _solver_config(self, max_cg_iterations=None, cg_tolerance=None,
-                       max_root_decomposition_size=None) -> dict:
-        ti = self._train_info
-        rank = max(int(self._training_result.lanczos_rank), _DEFAULT_PREDICT_LANCZOS_RANK)
-        if self.ard:
-            rank = max(rank, _DEFAULT_ARD_PREDICT_LANCZOS_RANK)
-        if max_root_decomposition_size is not None:
-            rank = int(max_root_decomposition_size)
-        rank = min(rank, self._X_train.shape[0])
-        return {
-            "max_cg_iterations": int(max_cg_iterations if max_cg_iterations is not None else
-                                     max(ti.get("max_cg_iterations", 0), _DEFAULT_PREDICT_MAX_CG_ITER)),
-            "cg_tolerance": float(cg_tolerance if cg_tolerance is not None else
-                                  min(ti.get("cg_tolerance", 1.0), _DEFAULT_PREDICT_CG_TOL)),
-            "max_root_decomposition_size": rank,
-        }
+                       max_root_decomposition_size=None, precond_rank=None) -> dict:
+        cfg = _prediction_solver_config(
+            self._train_info, int(self._training_result.lanczos_rank), is_ard=self.ard,
+            max_cg_iterations=max_cg_iterations, cg_tolerance=cg_tolerance,
+            precond_rank=precond_rank, max_root_decomposition_size=max_root_decomposition_size)
+        # A root cannot have more Lanczos vectors than training rows.
+        cfg["max_root_decomposition_size"] = min(cfg["max_root_decomposition_size"],
+                                                 self._X_train.shape[0])
+        return cfg
 
     def prepare_prediction_cache(self, variance_method: str = "love",
                                  max_root_decomposition_size: Optional[int] = None,
@@ -285,16 +315,15 @@ class SingleOutputGP:
         else:
             mean, var = cache.predict(Xt, return_var=want_var)
         if variance_method == "exact":
-            # predict_variance_exact_jit defaults: 300 iterations, tol 1e-3, the
-            # training preconditioner rank (gp.py:85-86).
+            # The exact route's solver settings (_prediction_solver_config):
+            # iterations max(training, 300), tolerance min(training, 1e-3), the
+            # training preconditioner rank.
             from .prediction import exact_variance
-            rank = preconditioner_rank if preconditioner_rank is not None else \
-                int(self._train_info.get("precond_rank", 0))
+            cfg = self._solver_config(max_cg_iterations, cg_tolerance, None, preconditioner_rank)
             var, _ = exact_variance(
-                self._provider, Xt,
-                max_cg_iter=max_cg_iterations if max_cg_iterations is not None else 300,
-                cg_tol=cg_tolerance if cg_tolerance is not None else 1e-3,
-                precond_rank=rank, block_cols=exact_prediction_block_cols or 0, comm=self._comm)
+                self._provider, Xt, max_cg_iter=cfg["max_cg_iterations"],
+                cg_tol=cfg["cg_tolerance"], precond_rank=cfg["precond_rank"],
+                block_cols=exact_prediction_block_cols or 0, comm=self._comm)
         if var is None:
             var = np.zeros_like(mean)
         std = np.sqrt(np.maximum(var, 0))
