@@ -7,7 +7,8 @@ It builds kernel trees with the reference API (mojogp.RBF, Matern*, RQ,
 Linear, Polynomial, +, *, scale, active_dims, make_ard_kernel), evaluates the
 float64 kernel matrix with KernelNode._evaluate_recursive
 (mojogp/kernel.py:756-923) on seeded inputs, and stores inputs, parameters,
-the tree description and K in tests/golden/kernels.npz. Inputs are chosen so
+the tree description, parameter names, default initial parameters, the engine
+parameter count and trainable mask, and K in tests/golden/kernels.npz / .json. Inputs are chosen so
 no Matern exponent reaches the -20 clamp, which the reference's NumPy
 evaluator does not apply but its generated GPU code does. Periodic is left
 out: the NumPy evaluator divides by l^2 while the generated GPU kernel
@@ -79,7 +80,10 @@ def main(ref_root: str) -> None:
         out[f"{name}__params"] = params
         out[f"{name}__K11"] = K11
         out[f"{name}__K12"] = K12
-        desc[name] = {"tree": describe(k), "param_names": k.get_param_names()}
+        desc[name] = {"tree": describe(k), "param_names": k.get_param_names(),
+                      "initial_params": [float(v) for v in k.get_initial_params()],
+                      "engine_num_params": int(k.engine_num_params()),
+                      "engine_trainable_mask": [bool(v) for v in k.engine_trainable_mask()]}
     here = Path(__file__).resolve().parent
     np.savez_compressed(here / "kernels.npz", **out)
     (here / "kernels.json").write_text(json.dumps(desc, indent=1, sort_keys=True))

@@ -54,3 +54,16 @@ def test_oracle_gradients_match_finite_differences(name):
         pm[p] -= h
         fd = (ok.kernel_matrix(spec, pp, X) - ok.kernel_matrix(spec, pm, X)) / (2 * h)
         np.testing.assert_allclose(G[p], fd, rtol=1e-5, atol=1e-7)
+
+
+@pytest.mark.parametrize("name", sorted(DESC))
+def test_default_parameters_and_trainable_mask_match_reference(name):
+    """Default initial parameters (KernelNode.get_initial_params) and which
+    parameters Adam moves (engine_trainable_mask, mojogp/kernel.py:482-492).
+    The reference's polynomial engine layout carries one hidden leading slot
+    (fixed variance), so only its public tail is compared."""
+    tree = KernelNode.from_dict(DESC[name]["tree"])
+    np.testing.assert_array_equal(tree.get_initial_params(), DESC[name]["initial_params"])
+    ref_mask = np.array(DESC[name]["engine_trainable_mask"])
+    ours = tree.engine_trainable_mask()
+    assert list(ours) == list(ref_mask[len(ref_mask) - len(ours):])
