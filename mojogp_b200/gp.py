@@ -33,6 +33,44 @@ _DEFAULT_PREDICT_MAX_CG_ITER = 300
 _DEFAULT_PREDICT_CG_TOL = 1e-3
 
 
+def _check_finite(name: str, a: np.ndarray) -> None:
+    if not np.all(np.isfinite(a)):
+        raise ValueError(f"{name} contains NaN or Inf values")
+
+
+def _check_training_controls(max_iterations, learning_rate, initial_noise) -> None:
+    """Optimiser argument checks with the reference's messages
+    (SingleOutputGP.fit, gp.py:1270-1276; the multi-output fits check the same
+    three, multi_output_gp.py:1555, 1613-1615, 4671-4675)."""
+    if max_iterations <= 0:
+        raise ValueError(f"max_iterations must be > 0, got {max_iterations}")
+    if learning_rate <= 0:
+        raise ValueError(f"learning_rate must be > 0, got {learning_rate}")
+    if initial_noise <= 0:
+        raise ValueError(f"initial_noise must be > 0, got {initial_noise}")
+
+
+def _check_multi_output_data(X: np.ndarray, Y: np.ndarray) -> None:
+    """Training data checks of the multi-output fits (multi_output_gp.py:1542-1553)."""
+    if X.ndim != 2:
+        raise ValueError(f"X must be 2D [n, d], got shape {X.shape}")
+    if Y.ndim != 2:
+        raise ValueError(f"Y must be 2D [n, T], got shape {Y.shape}")
+    if X.shape[0] != Y.shape[0]:
+        raise ValueError(f"X has {X.shape[0]} samples, Y has {Y.shape[0]} -- must match")
+    _check_finite("X", X)
+    _check_finite("Y", Y)
+
+
+def _check_test_inputs(Xt: np.ndarray, dim: int) -> None:
+    """Prediction input checks (multi_output_gp.py:2565-2573)."""
+    if Xt.ndim != 2:
+        raise ValueError(f"X_test must be 2D [m, d], got shape {Xt.shape}")
+    if Xt.shape[1] != dim:
+        raise ValueError(f"X_test has {Xt.shape[1]} features, expected {dim}")
+    _check_finite("X_test", Xt)
+
+
 def _prediction_lanczos_rank(rank_hint: Optional[int], is_ard: bool) -> int:
     """LOVE root rank: at least 100, at least 200 for ARD kernels
     (_prediction_lanczos_rank, gp.py:112-138, continuous kernels)."""
@@ -166,16 +204,26 @@ class SingleOutputGP:
         y = np.ascontiguousarray(y, dtype=np.float32)
         if X.ndim == 1:
             X = X[:, None]
+        # Data, then optimiser checks, with the reference's messages (gp.py:995-1004, 1266-1284).
         if X.ndim != 2:
-            raise ValueError(f"X must be 2D, got {X.ndim}D")
+            raise ValueError(f"X must be 2D, got shape {X.shape}")
         if y.ndim != 1:
-            raise ValueError(f"y must be 1D, got {y.ndim}D")
+            raise ValueError(f"y must be 1D, got shape {y.shape}")
         if X.shape[0] != y.shape[0]:
-            raise ValueError(f"X and y have different rows: {X.shape[0]} vs {y.shape[0]}")
+            raise ValueError(f"X has {X.shape[0]} samples, y has {y.shape[0]}")
         if X.shape[0] == 0:
             raise ValueError("cannot fit on an empty dataset")
-        if not (np.all(np.isfinite(X)) and np.all(np.isfinite(y))):
-            raise ValueError("X and y must be finite")
+        _check_finite("X", X)
+        _check_finite("y", y)
+        if preset is not None and preset not in self._PRESETS:
+            raise ValueError(f"Unknown preset '{preset}'. Must be one of: {list(self._PRESETS.keys())}")
+        _check_training_controls(max_iterations, learning_rate, initial_noise)
+        if early_stop_patience < 0:
+            raise ValueError(f"early_stop_patience must be >= 0, got {early_stop_patience}")
+        if early_stop_tol < 0:
+            raise ValueError(f"early_stop_tol must be >= 0, got {early_stop_tol}")
+        if prediction_cache_rank is not None and prediction_cache_rank <= 0:
+            raise ValueError("prediction_cache_rank must be positive or None")
         if method not in ("auto", "matrix_free", "mf", "materialized", "mat"):
             raise ValueError(f"method={method!r}: expected 'auto', 'matrix_free' or 'materialized'")
         # The materialized route (dense K + GEMM for n <= ~4e4) is served by the
@@ -183,7 +231,7 @@ class SingleOutputGP:
         # than streaming a stored K from HBM at t = 16 (fn_ptr_module.py:363-421).
         self._training_method = method
         if lr_schedule not in ("constant", "cosine"):
-            raise ValueError("lr_schedule must be 'constant' or 'cosine'")
+            raise ValueError(f"lr_schedule must be 'cosine' or 'constant', got '{lr_schedule}'")
         n, dim = X.shape
         self.dim = dim
         self._comm = comm
@@ -302,10 +350,9 @@ class SingleOutputGP:
         if variance_method not in ("love", "exact", "mean_only"):
             raise ValueError("variance_method must be one of 'love', 'exact', 'mean_only'")
         Xt = np.ascontiguousarray(X_test, dtype=np.float32)
-        if Xt.ndim == 1:
+        if Xt.ndim == 1 and self.dim == 1:
             Xt = Xt[:, None]
-        if Xt.shape[1] != self.dim:
-            raise ValueError(f"X_test has {Xt.shape[1]} features, expected {self.dim}")
+        _check_test_inputs(Xt, self.dim)
         want_var = variance_method == "love"
         cache = self.prepare_prediction_cache("love" if want_var else "mean_only",
                                               max_root_decomposition_size, max_cg_iterations,

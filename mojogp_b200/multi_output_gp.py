@@ -23,6 +23,7 @@ import numpy as np
 
 from . import _lib
 from .kernel import Kernel, KernelNode, make_ard_kernel
+from .gp import _check_multi_output_data, _check_test_inputs, _check_training_controls
 from .provider import Provider
 
 _STR = {"rbf": Kernel.rbf, "matern12": Kernel.matern12, "matern32": Kernel.matern32,
@@ -199,8 +200,8 @@ class MultiOutputLMCGP:
         if X.ndim == 1:
             X = X[:, None]
         Y = np.asarray(Y, np.float32)
-        if Y.ndim != 2 or Y.shape[0] != X.shape[0]:
-            raise ValueError("Y must be [n, T] with the rows of X")
+        _check_multi_output_data(X, Y)
+        _check_training_controls(max_iterations, learning_rate, initial_noise)
         n, d = X.shape
         T = Y.shape[1]
         R = self.num_latents
@@ -342,13 +343,14 @@ class MultiOutputLMCGP:
         4360-4519, with CG iterations max(max_cg_iterations, 100) and tolerance
         min(cg_tolerance, 1e-2)); 'mean_only' returns zero variance."""
         if self._lmc is None:
-            raise RuntimeError("model must be fit first")
+            raise RuntimeError("GP must be trained before prediction. Call fit() first.")
         if variance_method not in ("love", "exact", "mean_only"):
             raise ValueError("variance_method must be one of ('love', 'exact', 'mean_only'), "
                              f"got '{variance_method}'")
         Xt = np.ascontiguousarray(X_test, np.float32)
-        if Xt.ndim == 1:
+        if Xt.ndim == 1 and self.dim == 1:
             Xt = Xt[:, None]
+        _check_test_inputs(Xt, self.dim)
         T, n = self.T, self._X.shape[0]
         alpha = self._alpha.reshape(T, n).T  # [n, T]
         mean = np.zeros((Xt.shape[0], T))
@@ -477,8 +479,8 @@ class MultiOutputGP:
         if X.ndim == 1:
             X = X[:, None]
         Y = np.asarray(Y, np.float32)
-        if Y.ndim != 2 or Y.shape[0] != X.shape[0]:
-            raise ValueError("Y must be [n, T] with the rows of X")
+        _check_multi_output_data(X, Y)
+        _check_training_controls(max_iterations, learning_rate, initial_noise)
         n, d = X.shape
         T = Y.shape[1]
         R = T if self.task_rank < 0 else self.task_rank
@@ -623,12 +625,13 @@ class MultiOutputGP:
     def predict(self, X_test, return_var: bool = False, return_std: bool = False,
                 variance_method: str = "love", lanczos_rank: int = 0):
         if self._lmc is None:
-            raise RuntimeError("model must be fit first")
+            raise RuntimeError("GP must be trained before prediction. Call fit() first.")
         if variance_method not in ("love", "exact", "mean_only"):
             raise ValueError("variance_method must be one of 'love', 'exact', 'mean_only'")
         Xt = np.ascontiguousarray(X_test, np.float32)
-        if Xt.ndim == 1:
+        if Xt.ndim == 1 and self.dim == 1:
             Xt = Xt[:, None]
+        _check_test_inputs(Xt, self.dim)
         T, n = self.T, self._X.shape[0]
         prov = self._lmc.providers[0]
         alpha = self._alpha.reshape(T, n).T

@@ -1,0 +1,95 @@
+"""Public-API argument contracts that hold before any device work (CPU): the
+reference's validation order and messages for the fits
+(mojogp/gp.py:995-1004, 1266-1284; multi_output_gp.py:1542-1615, 4659-4675)
+and the untrained-predict error. Restated from the reference's contract tests
+(tests/unit/test_gp_wrapper_api_contracts.py:44-100)."""
+import numpy as np
+import pytest
+
+from mojogp_b200.gp import SingleOutputGP
+from mojogp_b200.kernel import RBF
+from mojogp_b200.multi_output_gp import MultiOutputGP, MultiOutputLMCGP
+
+
+@pytest.fixture
+def data():
+    rng = np.random.default_rng(0)
+    X = rng.uniform(-1, 1, size=(40, 2)).astype(np.float32)
+    Y = rng.standard_normal((40, 3)).astype(np.float32)
+    return X, Y
+
+
+def _models():
+    return [("icm", lambda: MultiOutputGP(kernel="rbf")),
+            ("lmc", lambda: MultiOutputLMCGP(kernels=["rbf"]))]
+
+
+@pytest.mark.parametrize("name,make", _models())
+def test_multi_output_rejects_non_finite_data(data, name, make):
+    X, Y = data
+    Xb = X.copy()
+    Xb[0, 0] = np.nan
+    with pytest.raises(ValueError, match="X contains NaN or Inf"):
+        make().fit(Xb, Y, max_iterations=5)
+    Yb = Y.copy()
+    Yb[1, 2] = np.inf
+    with pytest.raises(ValueError, match="Y contains NaN or Inf"):
+        make().fit(X, Yb, max_iterations=5)
+
+
+@pytest.mark.parametrize("name,make", _models())
+@pytest.mark.parametrize("kw,msg", [({"initial_noise": -0.1}, "initial_noise must be > 0"),
+                                    ({"learning_rate": 0.0}, "learning_rate must be > 0"),
+                                    ({"learning_rate": -0.01}, "learning_rate must be > 0"),
+                                    ({"max_iterations": 0}, "max_iterations must be > 0")])
+def test_multi_output_rejects_bad_controls(data, name, make, kw, msg):
+    X, Y = data
+    with pytest.raises(ValueError, match=msg):
+        make().fit(X, Y, **kw)
+
+
+@pytest.mark.parametrize("name,make", _models())
+def test_multi_output_shape_checks(data, name, make):
+    X, Y = data
+    with pytest.raises(ValueError, match="Y must be 2D"):
+        make().fit(X, Y[:, 0])
+    with pytest.raises(ValueError, match="samples"):
+        make().fit(X, Y[:30])
+
+
+@pytest.mark.parametrize("name,make", _models())
+def test_multi_output_predict_before_fit(data, name, make):
+    with pytest.raises(RuntimeError, match="trained"):
+        make().predict(data[0])
+
+
+def test_single_output_contracts(data):
+    X, Y = data
+    y = Y[:, 0]
+    gp = SingleOutputGP(RBF())
+    with pytest.raises(ValueError, match="X contains NaN or Inf"):
+        Xb = X.copy()
+        Xb[3, 1] = np.inf
+        gp.fit(Xb, y)
+    with pytest.raises(ValueError, match="y contains NaN or Inf"):
+        yb = y.copy()
+        yb[0] = np.nan
+        gp.fit(X, yb)
+    with pytest.raises(ValueError, match="samples"):
+        gp.fit(X, y[:10])
+    with pytest.raises(ValueError, match="y must be 1D"):
+        gp.fit(X, Y)
+    with pytest.raises(ValueError, match="max_iterations must be > 0"):
+        gp.fit(X, y, max_iterations=0)
+    with pytest.raises(ValueError, match="learning_rate must be > 0"):
+        gp.fit(X, y, learning_rate=0.0)
+    with pytest.raises(ValueError, match="initial_noise must be > 0"):
+        gp.fit(X, y, initial_noise=-0.1)
+    with pytest.raises(ValueError, match="Unknown preset"):
+        gp.fit(X, y, preset="turbo")
+    with pytest.raises(ValueError, match="lr_schedule"):
+        gp.fit(X, y, lr_schedule="linear")
+    with pytest.raises(ValueError, match="method"):
+        gp.fit(X, y, method="bogus")
+    with pytest.raises(RuntimeError):
+        gp.predict(X)
