@@ -202,8 +202,6 @@ class SingleOutputGP:
         """Train hyperparameters by BBMM (mBCG + SLQ) with Adam on the GPU."""
         X = np.ascontiguousarray(X, dtype=np.float32)
         y = np.ascontiguousarray(y, dtype=np.float32)
-        if X.ndim == 1:
-            X = X[:, None]
         # Data, then optimiser checks, with the reference's messages (gp.py:995-1004, 1266-1284).
         if X.ndim != 2:
             raise ValueError(f"X must be 2D, got shape {X.shape}")
@@ -386,14 +384,19 @@ class SingleOutputGP:
             raise RuntimeError("GP must be trained first.")
         return -float(self._training_result.nll)
 
-    def get_params(self) -> dict:
+    def get_learned_params(self) -> dict:
+        """Learned kernel parameters by name, then noise and mean
+        (get_learned_params, gp.py:3072-3099, homoskedastic noise)."""
         if not self._is_trained:
-            raise RuntimeError("GP must be trained first.")
+            raise RuntimeError("Model must be trained before getting params")
         tr = self._training_result
         out = dict(zip(self.kernel.get_param_names(), map(float, tr.params)))
         out["noise"] = float(tr.noise)
         out["mean"] = float(tr.mean)
         return out
+
+    def get_params(self) -> dict:
+        return self.get_learned_params()
 
     @property
     def noise(self) -> float:

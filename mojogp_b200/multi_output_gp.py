@@ -197,8 +197,6 @@ class MultiOutputLMCGP:
             raise ValueError(f"method={method!r}: expected 'matrix_free' or 'materialized'")
         # "materialized" is served by the matrix-free operator (see SingleOutputGP.fit).
         X = np.ascontiguousarray(X, np.float32)
-        if X.ndim == 1:
-            X = X[:, None]
         Y = np.asarray(Y, np.float32)
         _check_multi_output_data(X, Y)
         _check_training_controls(max_iterations, learning_rate, initial_noise)
@@ -476,8 +474,6 @@ class MultiOutputGP:
             raise ValueError(f"method={method!r}: expected 'matrix_free' or 'materialized'")
         # "materialized" is served by the matrix-free operator (see SingleOutputGP.fit).
         X = np.ascontiguousarray(X, np.float32)
-        if X.ndim == 1:
-            X = X[:, None]
         Y = np.asarray(Y, np.float32)
         _check_multi_output_data(X, Y)
         _check_training_controls(max_iterations, learning_rate, initial_noise)

@@ -55,6 +55,8 @@ def test_multi_output_shape_checks(data, name, make):
         make().fit(X, Y[:, 0])
     with pytest.raises(ValueError, match="samples"):
         make().fit(X, Y[:30])
+    with pytest.raises(ValueError, match="X must be 2D"):
+        make().fit(X[:, 0], Y)
 
 
 @pytest.mark.parametrize("name,make", _models())
@@ -77,6 +79,8 @@ def test_single_output_contracts(data):
         gp.fit(X, yb)
     with pytest.raises(ValueError, match="samples"):
         gp.fit(X, y[:10])
+    with pytest.raises(ValueError, match="2D"):
+        gp.fit(X[:, 0], y)
     with pytest.raises(ValueError, match="y must be 1D"):
         gp.fit(X, Y)
     with pytest.raises(ValueError, match="max_iterations must be > 0"):
@@ -91,5 +95,7 @@ def test_single_output_contracts(data):
         gp.fit(X, y, lr_schedule="linear")
     with pytest.raises(ValueError, match="method"):
         gp.fit(X, y, method="bogus")
-    with pytest.raises(RuntimeError):
+    with pytest.raises(RuntimeError, match="trained"):
         gp.predict(X)
+    with pytest.raises(RuntimeError, match="trained"):
+        gp.get_learned_params()
