@@ -43,6 +43,67 @@ def _dsp(x):
     return 1.0 / (1.0 + math.exp(-x)) if x > -20 else math.exp(x)
 
 
+def build_lmc_initial_params_from_lengthscales(kernels, initial_lengthscales) -> np.ndarray:
+    """Flat LMC initial parameters from lengthscales: each latent's lengthscale
+    slots take the given values, every other parameter 1
+    (_build_lmc_initial_params_from_lengthscales, multi_output_gp.py:231-284).
+    Accepted shapes: (R,) when every latent has one lengthscale, (total,) in
+    latent order, or (R, c) when every latent has c lengthscales."""
+    values = np.asarray(initial_lengthscales, dtype=np.float32)
+    idx = [[i for i, nm in enumerate(k.get_param_names())
+            if nm.endswith("_lengthscale") or "_ls_" in nm] for k in kernels]
+    counts = [len(ix) for ix in idx]
+    total = sum(counts)
+    R = len(kernels)
+    if total == 0:
+        raise ValueError("initial_lengthscales was provided, but no latent has lengthscale parameters")
+    if values.shape == (R,) and all(c == 1 for c in counts):
+        per = [values[s:s + 1] for s in range(R)]
+    elif values.shape == (total,):
+        per, off = [], 0
+        for c in counts:
+            per.append(values[off:off + c])
+            off += c
+    elif len(set(counts)) == 1 and values.shape == (R, counts[0]):
+        per = [values[s] for s in range(R)]
+    else:
+        shapes = [f"({total},)"]
+        if all(c == 1 for c in counts):
+            shapes.append(f"({R},)")
+        if len(set(counts)) == 1:
+            shapes.append(f"({R}, {counts[0]})")
+        raise ValueError("initial_lengthscales must have shape " + " or ".join(shapes)
+                         + f" for per-latent lengthscale counts {counts}, got {values.shape}")
+    out = []
+    for k, ix, vals in zip(kernels, idx, per):
+        p = np.ones(k.num_params(), dtype=np.float32)
+        p[ix] = vals
+        out.append(p)
+    return np.concatenate(out).astype(np.float32)
+
+
+def _split_latent_params(kernels, initial_params, initial_lengthscales) -> list:
+    """Per-latent starting parameters: the kernels' defaults, or a flat vector
+    (given, or built from lengthscales) split in latent order."""
+    if initial_params is None and initial_lengthscales is None:
+        return [k.get_initial_params() for k in kernels]
+    if initial_params is None:
+        flat = build_lmc_initial_params_from_lengthscales(kernels, initial_lengthscales)
+    else:
+        flat = np.asarray(initial_params, dtype=np.float32).ravel()
+    sizes = [k.num_params() for k in kernels]
+    if flat.shape[0] != sum(sizes):
+        raise ValueError(f"initial_params has {flat.shape[0]} values, expected {sum(sizes)} "
+                         f"(per-latent counts {sizes})")
+    if not np.all(np.isfinite(flat)) or np.any(flat <= 0):
+        raise ValueError("initial parameters must be finite and > 0")
+    out, off = [], 0
+    for sz in sizes:
+        out.append(flat[off:off + sz].copy())
+        off += sz
+    return out
+
+
 class LMC:
     """Thin owner of a gpb_lmc handle over R providers."""
 
@@ -192,7 +253,11 @@ class MultiOutputLMCGP:
 
     def fit(self, X, Y, max_iterations: int = 100, learning_rate: float = 0.05,
             initial_noise: float = 0.1, method: str = "matrix_free", verbose: bool = False,
-            comm=None):
+            initial_params=None, initial_lengthscales=None, comm=None):
+        """initial_params: the latents' public parameters concatenated in
+        latent order; initial_lengthscales: lengthscales only, the other
+        parameters at 1 (_build_lmc_initial_params_from_lengthscales,
+        multi_output_gp.py:231-284); at most one of the two."""
         if method not in ("matrix_free", "mf", "auto", "materialized", "mat"):
             raise ValueError(f"method={method!r}: expected 'matrix_free' or 'materialized'")
         # "materialized" is served by the matrix-free operator (see SingleOutputGP.fit).
@@ -200,14 +265,16 @@ class MultiOutputLMCGP:
         Y = np.asarray(Y, np.float32)
         _check_multi_output_data(X, Y)
         _check_training_controls(max_iterations, learning_rate, initial_noise)
+        if initial_params is not None and initial_lengthscales is not None:
+            raise ValueError("Provide initial_params or initial_lengthscales, not both")
         n, d = X.shape
         T = Y.shape[1]
         R = self.num_latents
-        self.T, self.dim = T, d
-        self._X = X
         self.kernels_resolved = [make_ard_kernel(k, d) if self.ard else k.resolve_ard(d)
                                  for k in self.kernels]
-        params0 = [k.get_initial_params() for k in self.kernels_resolved]
+        params0 = _split_latent_params(self.kernels_resolved, initial_params, initial_lengthscales)
+        self.T, self.dim = T, d
+        self._X = X
         masks = [k.engine_trainable_mask() for k in self.kernels_resolved]
         provs = [Provider(X, k, p, 0.0, device=self.device)
                  for k, p in zip(self.kernels_resolved, params0)]

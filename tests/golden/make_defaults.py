@@ -6,10 +6,14 @@ Run where the reference checkout is importable:
 It records SingleOutputGP._PRESETS (mojogp/gp.py:790-818), the LOVE rank rule
 _prediction_lanczos_rank (gp.py:112-138) and the prediction solver settings
 _prediction_solver_config (gp.py:141-199) for continuous (not mixed) kernels
-on a grid of training settings and overrides, into tests/golden/defaults.json.
+on a grid of training settings and overrides, and the LMC initial parameters
+built from lengthscales (_build_lmc_initial_params_from_lengthscales,
+multi_output_gp.py:231-284), into tests/golden/defaults.json.
 """
 import itertools
 import json
+
+import numpy as np
 import sys
 from pathlib import Path
 
@@ -33,6 +37,32 @@ def main(ref: str) -> None:
                                           is_ard=ard, **ov)
         out["solver_config"].append({"train_info": ti, "overrides": ov, "rank_hint": hint,
                                      "is_ard": ard, "config": cfg})
+    # LMC initial parameters from lengthscales (multi_output_gp.py:231-284).
+    from mojogp import Kernel
+    from mojogp.kernel import make_ard_kernel
+    from mojogp.multi_output_gp import _build_lmc_initial_params_from_lengthscales as build
+
+    def make(spec, d, ard):
+        ks = []
+        for name, dims in spec:
+            k = getattr(Kernel, name)(active_dims=dims) if dims else getattr(Kernel, name)()
+            ks.append(make_ard_kernel(k, d) if ard else k)
+        return ks
+
+    lmc_cases = [
+        ([("rbf", None), ("matern52", None)], 3, False, [0.4, 1.7]),
+        ([("rbf", [0, 2]), ("matern52", [1, 3, 4])], 5, True, [0.2, 0.3, 1.1, 1.2, 1.3]),
+        ([("rbf", None), ("matern32", None)], 3, True, [[0.5, 0.6, 0.7], [1.5, 1.6, 1.7]]),
+        ([("rbf", None), ("rq", None), ("linear", None)], 2, False, [0.5, 0.9]),
+        ([("rbf", [0, 2]), ("matern52", [1, 3, 4])], 5, True, [[1.0, 1.0], [1.0, 1.0]]),
+    ]
+    out["lmc_lengthscales"] = []
+    for spec, d, ard, vals in lmc_cases:
+        try:
+            res = {"params": [float(v) for v in build(make(spec, d, ard), np.asarray(vals))]}
+        except ValueError as e:
+            res = {"error": str(e)}
+        out["lmc_lengthscales"].append({"kernels": spec, "d": d, "ard": ard, "values": vals, **res})
     here = Path(__file__).resolve().parent
     (here / "defaults.json").write_text(json.dumps(out, indent=1, sort_keys=True))
     print("wrote", here / "defaults.json")
