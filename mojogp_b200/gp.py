@@ -71,6 +71,56 @@ def _check_test_inputs(Xt: np.ndarray, dim: int) -> None:
     _check_finite("X_test", Xt)
 
 
+def _resolve_fit_route(method: str, n: int, dim: int, single_type, ard: bool,
+                       learning_rate: float, default_params: bool, params: np.ndarray,
+                       preconditioner, preconditioner_rank, use_preconditioner,
+                       precond_rebuild_threshold) -> dict:
+    """Training route and the defaults it implies (SingleOutputGP.fit,
+    gp.py:1350-1468, continuous kernels). "auto" is the dense route up to 2000
+    rows; the dense route (served here by the same matrix-free kernels) starts
+    a 1-D RBF at lengthscale <= 0.5, picks greedy pivots for Matérn-3/2, no
+    preconditioner for Linear, and rebuild threshold 0.1 for ARD stationary
+    leaves; the matrix-free route starts a low-d isotropic RBF at <= 0.6 (n >=
+    10000) and preconditions only that case (rank 256, n >= 5000) unless the
+    caller asked. `single_type` is the KernelType of a one-leaf kernel, else
+    None. Returns method, params, preconditioner, precond_rank (None = the
+    preset's) and precond_rebuild_threshold."""
+    if method in ("materialized", "mat"):
+        route = "materialized"
+    elif method == "auto":
+        route = "materialized" if n <= 2000 else "matrix_free"
+    else:
+        route = "matrix_free"
+    p = np.asarray(params, np.float32).copy()
+    rbf = single_type == KernelType.RBF
+    if default_params and route == "materialized" and learning_rate <= 0.05 and rbf and dim == 1 \
+            and p.shape[0] >= 1:
+        p[0] = min(float(p[0]), 0.5)
+    if default_params and route == "matrix_free" and learning_rate <= 0.05 and rbf and not ard \
+            and 1 < dim <= 8 and n >= 10000 and p.shape[0] >= 1:
+        p[0] = min(float(p[0]), 0.6)
+    explicit = (preconditioner is not None or preconditioner_rank is not None
+                or use_preconditioner is not None)
+    precond, rank = preconditioner, preconditioner_rank
+    if precond is None and route == "materialized" and learning_rate <= 0.05 \
+            and single_type == KernelType.MATERN32:
+        precond = "greedy"
+    if not explicit and route == "materialized" and single_type == KernelType.LINEAR:
+        rank = 0
+    if not explicit and route == "matrix_free":
+        if rbf and not ard and 1 < dim <= 8 and n >= 5000:
+            precond, rank = "greedy", 256
+        else:
+            rank = 0
+    thr = precond_rebuild_threshold
+    if thr is None and route == "materialized" and ard and single_type in (
+            KernelType.RBF, KernelType.MATERN12, KernelType.MATERN32, KernelType.MATERN52,
+            KernelType.RQ):
+        thr = 0.1
+    return {"method": route, "params": p, "preconditioner": precond, "precond_rank": rank,
+            "precond_rebuild_threshold": thr}
+
+
 def _prediction_lanczos_rank(rank_hint: Optional[int], is_ard: bool) -> int:
     """LOVE root rank: at least 100, at least 200 for ARD kernels
     (_prediction_lanczos_rank, gp.py:112-138, continuous kernels)."""
@@ -227,7 +277,6 @@ class SingleOutputGP:
         # The materialized route (dense K + GEMM for n <= ~4e4) is served by the
         # matrix-free tile kernels: re-evaluating K on the tensor cores costs less
         # than streaming a stored K from HBM at t = 16 (fn_ptr_module.py:363-421).
-        self._training_method = method
         if lr_schedule not in ("constant", "cosine"):
             raise ValueError(f"lr_schedule must be 'cosine' or 'constant', got '{lr_schedule}'")
         n, dim = X.shape
@@ -240,20 +289,15 @@ class SingleOutputGP:
                   else np.asarray(initial_params, np.float32).ravel())
         if params.shape[0] != P:
             raise ValueError(f"initial_params must have {P} entries, got {params.shape[0]}")
-        params = params.astype(np.float32).copy()
-        # gp.py:1376-1408: milder lengthscale start for large low-d matrix-free RBF
-        if (default_params and learning_rate <= 0.05 and self._single_type(KernelType.RBF)
-                and not self.ard and 1 < dim <= 8 and n >= 10000):
-            params[0] = min(float(params[0]), 0.6)
-        # gp.py:1437-1457: matrix-free preconditioner defaults
-        explicit = (preconditioner is not None or preconditioner_rank is not None
-                    or use_preconditioner is not None)
-        rank = preconditioner_rank
-        if not explicit:
-            if self._single_type(KernelType.RBF) and not self.ard and 1 < dim <= 8 and n >= 5000:
-                preconditioner, rank = "greedy", 256
-            else:
-                rank = 0
+        k = self.kernel_spec
+        route = _resolve_fit_route(method, n, dim, k.kernel_type if k.is_leaf() else None,
+                                   self.ard, learning_rate, default_params, params, preconditioner,
+                                   preconditioner_rank, use_preconditioner,
+                                   precond_rebuild_threshold)
+        self._training_method = route["method"]
+        params = route["params"]
+        preconditioner, rank = route["preconditioner"], route["precond_rank"]
+        precond_rebuild_threshold = route["precond_rebuild_threshold"]
         if preconditioner not in (None, "greedy"):
             raise NotImplementedError(
                 f"preconditioner={preconditioner!r}: only the greedy pivoted Cholesky is built")

@@ -99,3 +99,46 @@ def test_single_output_contracts(data):
         gp.predict(X)
     with pytest.raises(RuntimeError, match="trained"):
         gp.get_learned_params()
+
+
+def _route(method, n, dim, kt, ard=False, lr=0.01, default=True, **kw):
+    from mojogp_b200.gp import _resolve_fit_route
+    args = dict(preconditioner=None, preconditioner_rank=None, use_preconditioner=None,
+                precond_rebuild_threshold=None)
+    args.update(kw)
+    return _resolve_fit_route(method, n, dim, kt, ard, lr, default,
+                              np.ones(3, np.float32), **args)
+
+
+def test_fit_route_defaults_follow_the_reference():
+    """SingleOutputGP.fit's route resolution and route defaults
+    (mojogp/gp.py:1350-1468)."""
+    from mojogp_b200.kernel import KernelType as K
+    # auto: the dense route up to 2000 rows
+    assert _route("auto", 2000, 1, K.RBF)["method"] == "materialized"
+    assert _route("auto", 2001, 1, K.RBF)["method"] == "matrix_free"
+    assert _route("mat", 10, 1, K.RBF)["method"] == "materialized"
+    # dense 1-D RBF starts at lengthscale 0.5; the preset's preconditioner rank
+    r = _route("materialized", 500, 1, K.RBF)
+    assert r["params"][0] == np.float32(0.5) and r["precond_rank"] is None
+    assert _route("materialized", 500, 1, K.RBF, lr=0.1)["params"][0] == 1.0
+    assert _route("materialized", 500, 1, K.RBF, default=False)["params"][0] == 1.0
+    assert _route("materialized", 500, 2, K.RBF)["params"][0] == 1.0
+    # dense Matérn-3/2 greedy; dense Linear unpreconditioned; dense ARD threshold 0.1
+    assert _route("materialized", 500, 2, K.MATERN32)["preconditioner"] == "greedy"
+    assert _route("materialized", 500, 2, K.LINEAR)["precond_rank"] == 0
+    assert _route("materialized", 500, 2, K.LINEAR, preconditioner_rank=7)["precond_rank"] == 7
+    assert _route("materialized", 500, 3, K.MATERN52, ard=True)["precond_rebuild_threshold"] == 0.1
+    assert _route("materialized", 500, 3, None, ard=True)["precond_rebuild_threshold"] is None
+    # matrix-free: low-d isotropic RBF gets the milder start and rank 256 ...
+    r = _route("matrix_free", 20000, 4, K.RBF)
+    assert r["params"][0] == np.float32(0.6)
+    assert (r["preconditioner"], r["precond_rank"]) == ("greedy", 256)
+    r = _route("matrix_free", 6000, 4, K.RBF)
+    assert r["params"][0] == 1.0 and r["precond_rank"] == 256
+    # ... everything else runs unpreconditioned unless asked
+    assert _route("matrix_free", 20000, 9, K.RBF)["precond_rank"] == 0
+    assert _route("matrix_free", 20000, 4, K.RBF, ard=True)["precond_rank"] == 0
+    assert _route("matrix_free", 20000, 4, K.MATERN52)["precond_rank"] == 0
+    assert _route("matrix_free", 20000, 4, K.MATERN52, preconditioner="greedy")["precond_rank"] is None
+    assert _route("matrix_free", 20000, 4, K.RBF, use_preconditioner=False)["precond_rank"] is None

@@ -76,10 +76,13 @@ def test_input_validation(gpb_lib):
 
 def test_materialized_route_name_is_served(gpb_lib):
     """method="materialized" (the reference's dense route) runs the matrix-free
-    kernels and gives the same fit."""
+    kernels: with the dense route's defaults (here the preset's rank-100 greedy
+    preconditioner, gp.py:1409-1468) spelled out, the matrix-free route gives
+    the same fit, bit for bit."""
     rng = np.random.default_rng(4)
     X = rng.uniform(-2, 2, size=(300, 2)).astype(np.float32)
     y = (np.sin(X[:, 0]) + 0.1 * rng.standard_normal(300)).astype(np.float32)
     a = SingleOutputGP(RBF()).fit(X, y, max_iterations=5, method="materialized")
-    b = SingleOutputGP(RBF()).fit(X, y, max_iterations=5, method="matrix_free")
+    b = SingleOutputGP(RBF()).fit(X, y, max_iterations=5, method="matrix_free",
+                                  preconditioner_rank=100)
     np.testing.assert_allclose(a.nll_history, b.nll_history, rtol=0, atol=0)
