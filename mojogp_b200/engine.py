@@ -129,3 +129,105 @@ def bbmm(provider: Provider, y_centered: np.ndarray, *, num_probes: int = 10,
               iteration, C.byref(nll), _p(grads), C.byref(ld), C.byref(iq), C.byref(it))
     return {"nll": nll.value, "grads": grads, "logdet": ld.value, "inv_quad": iq.value,
             "cg_iters": it.value}
+
+
+PREDICT_MEAN_ONLY, PREDICT_LOVE, PREDICT_EXACT = 0, 1, 2
+_DEFAULT_LOVE_RANK, _DEFAULT_ARD_LOVE_RANK = 100, 200
+
+
+def predict(info, y, x_test, params, final_noise: float, final_mean: float,
+            variance_method: int, max_cg_iter: int = 100, cg_tol: float = 1e-2,
+            precond_rank: int = 10, lanczos_rank: int = 0, provider_state_current: bool = False,
+            exact_block_cols: int = 0, cached_alpha=None, cached_love_root=None, test_info=None,
+            *, comm=None) -> dict:
+    """Engine-level prediction with the reference binding's positional arguments
+    and result keys (predict, jit_engine_bindings.mojo:944-1234).
+
+    Unless `provider_state_current`, the provider takes `params` and
+    `final_noise` first. alpha = (K + noise I)^{-1} (y - final_mean) by CG
+    (`max_cg_iter`, `cg_tol`), or `cached_alpha`. variance_method 0: mean only;
+    1: LOVE with a root of `lanczos_rank` vectors (<= 0: 100, 200 for ARD
+    kernels; _resolve_exact_predict_lanczos_rank,
+    jit_engine_binding_helpers.mojo:23-45), or `cached_love_root` [rank * n];
+    2: CG-exact variance (blocks of `exact_block_cols`, preconditioner rank
+    `precond_rank`). Variances include the noise. The result carries
+    `cached_alpha` / `cached_lanczos_root` when they were computed here, for the
+    caller to pass back. `test_info` is accepted for signature compatibility:
+    test-point diagonals come from the training provider's kernel.
+    """
+    import time
+
+    from . import prediction
+
+    if variance_method not in (PREDICT_MEAN_ONLY, PREDICT_LOVE, PREDICT_EXACT):
+        raise ValueError(f"variance_method must be 0, 1 or 2, got {variance_method}")
+    prov = info["provider"] if isinstance(info, dict) else info
+    n = prov.n
+    Xt = np.ascontiguousarray(x_test, dtype=np.float32)
+    if Xt.ndim == 1:
+        Xt = Xt[:, None]
+    t_start = time.perf_counter()
+    if not provider_state_current:
+        prov.update_params(np.asarray(params, dtype=np.float32))
+        prov.update_noise(float(final_noise))
+    t0 = time.perf_counter()
+    alpha_cache_used = cached_alpha is not None
+    if alpha_cache_used:
+        alpha = np.ascontiguousarray(cached_alpha, dtype=np.float32).ravel()
+        if alpha.shape[0] != n:
+            raise ValueError(f"cached alpha has {alpha.shape[0]} values, expected {n}")
+    else:
+        yc = np.ascontiguousarray(y, dtype=np.float32).ravel() - np.float32(final_mean)
+        alpha, _ = prediction.compute_alpha(prov, yc, max_cg_iter, cg_tol, comm=comm)
+    alpha_s = time.perf_counter() - t0
+    rank, root, root_cached = 0, None, False
+    if variance_method == PREDICT_LOVE:
+        is_ard = bool(info.get("is_ard", False)) if isinstance(info, dict) else False
+        rank = lanczos_rank if lanczos_rank > 0 else (
+            _DEFAULT_ARD_LOVE_RANK if is_ard else _DEFAULT_LOVE_RANK)
+        rank = min(rank, n)
+        if cached_love_root is not None:
+            r = np.ascontiguousarray(cached_love_root, dtype=np.float32).ravel()
+            if r.shape[0] == n * rank:
+                root, root_cached = r.reshape(rank, n), True
+    t1 = time.perf_counter()
+    cache = prediction.PredictionCache(prov, alpha, float(final_mean), rank, root=root, comm=comm)
+    root_s = time.perf_counter() - t1 if (rank > 0 and not root_cached) else 0.0
+    try:
+        t2 = time.perf_counter()
+        mean, var = cache.predict(Xt, return_var=variance_method == PREDICT_LOVE)
+        mean_s = time.perf_counter() - t2
+        exact_iters = 0
+        var_s = 0.0  # LOVE: the variance comes out of the same cross-product pass as the mean
+        if variance_method == PREDICT_EXACT:
+            t3 = time.perf_counter()
+            var, exact_iters = prediction.exact_variance(prov, Xt, max_cg_iter, cg_tol,
+                                                         precond_rank, exact_block_cols,
+                                                         comm=comm)
+            var_s = time.perf_counter() - t3
+        root_out = cache.root() if (variance_method == PREDICT_LOVE and not root_cached) else None
+    finally:
+        cache.destroy()
+    m = Xt.shape[0]
+    if var is None:
+        var = np.zeros(m, np.float32)
+    var = np.asarray(var, dtype=np.float32)
+    out = {
+        "mean": np.asarray(mean, dtype=np.float32),
+        "variance": var,
+        "std": np.sqrt(np.maximum(var, 0)).astype(np.float32),
+        "alpha_time_s": alpha_s,
+        "mean_time_s": mean_s,
+        "variance_time_s": var_s,
+        "love_root_time_s": root_s,
+        "total_time_s": time.perf_counter() - t_start,
+        "exact_cg_total_iterations": int(exact_iters),
+        "provider_state_update_skipped": bool(provider_state_current),
+        "alpha_cache_used": alpha_cache_used,
+        "love_root_cache_used": root_cached,
+    }
+    if not alpha_cache_used:
+        out["cached_alpha"] = alpha
+    if root_out is not None:
+        out["cached_lanczos_root"] = root_out.ravel()
+    return out

@@ -1,0 +1,122 @@
+"""engine.predict's orchestration (the reference binding's argument handling
+and result keys, jit_engine_bindings.mojo:944-1234) with stand-ins for the
+device calls (CPU): which provider updates, solves and caches run for each
+variance method and cache argument, and the keys that come back."""
+import inspect
+
+import numpy as np
+import pytest
+
+from mojogp_b200 import engine, prediction
+
+
+class _Prov:
+    n = 6
+
+    def __init__(self):
+        self.calls = []
+
+    def update_params(self, p):
+        self.calls.append(("params", np.asarray(p).tolist()))
+
+    def update_noise(self, s):
+        self.calls.append(("noise", s))
+
+
+class _Cache:
+    made = []
+
+    def __init__(self, provider, alpha, mean, love_rank, root=None, comm=None):
+        _Cache.made.append(dict(alpha=np.asarray(alpha), mean=mean, rank=love_rank, root=root))
+        self.rank, self.n = love_rank, provider.n
+        self.destroyed = False
+
+    def predict(self, Xt, return_var=True):
+        m = Xt.shape[0]
+        return np.full(m, 1.5, np.float32), (np.full(m, 0.25, np.float32)
+                                             if (return_var and self.rank > 0) else None)
+
+    def root(self):
+        return np.arange(self.rank * self.n, dtype=np.float32).reshape(self.rank, self.n)
+
+    def destroy(self):
+        self.destroyed = True
+
+
+@pytest.fixture
+def stubs(monkeypatch):
+    log = {}
+
+    def compute_alpha(provider, y_centered, max_cg_iter=300, cg_tol=1e-3, comm=None):
+        log["alpha"] = (np.asarray(y_centered).tolist(), max_cg_iter, cg_tol)
+        return np.full(provider.n, 2.0, np.float32), 7
+
+    def exact_variance(provider, X_test, max_cg_iter=300, cg_tol=1e-3, precond_rank=0,
+                       block_cols=0, comm=None):
+        log["exact"] = (max_cg_iter, cg_tol, precond_rank, block_cols)
+        return np.full(X_test.shape[0], 0.5, np.float32), 11
+
+    # The stand-ins take the real functions' parameters, in order.
+    names = lambda f: list(inspect.signature(f).parameters)
+    assert names(compute_alpha) == names(prediction.compute_alpha)
+    assert names(exact_variance) == names(prediction.exact_variance)
+    assert names(_Cache.__init__) == names(prediction.PredictionCache.__init__)
+    monkeypatch.setattr(prediction, "compute_alpha", compute_alpha)
+    monkeypatch.setattr(prediction, "exact_variance", exact_variance)
+    monkeypatch.setattr(prediction, "PredictionCache", _Cache)
+    _Cache.made = []
+    return log
+
+
+def _info(ard=False):
+    return {"provider": _Prov(), "n": 6, "is_ard": ard}
+
+
+def test_love_route_computes_alpha_and_root(stubs):
+    info = _info()
+    y = np.arange(6, dtype=np.float32)
+    out = engine.predict(info, y, np.zeros((3, 2)), np.array([0.5, 1.0]), 0.1, 2.0, 1, 50, 1e-3)
+    assert info["provider"].calls == [("params", [0.5, 1.0]), ("noise", 0.1)]
+    assert stubs["alpha"] == ((y - 2.0).tolist(), 50, 1e-3)
+    assert _Cache.made[0]["rank"] == 6  # default 100 capped at n
+    assert out["mean"].tolist() == [1.5] * 3 and out["variance"].tolist() == [0.25] * 3
+    np.testing.assert_allclose(out["std"], 0.5)
+    assert out["cached_alpha"].tolist() == [2.0] * 6
+    assert out["cached_lanczos_root"].shape == (36,)
+    assert not out["alpha_cache_used"] and not out["love_root_cache_used"]
+    for k in ("alpha_time_s", "mean_time_s", "variance_time_s", "love_root_time_s",
+              "total_time_s", "provider_state_update_skipped"):
+        assert k in out
+
+
+def test_caches_and_state_flags_are_honoured(stubs):
+    info = _info()
+    root = np.ones(6 * 4, np.float32)
+    out = engine.predict(info, np.zeros(6), np.zeros((2, 2)), [1.0, 1.0], 0.1, 0.0, 1, 100, 1e-2,
+                         10, 4, True, 0, np.full(6, 3.0), root)
+    assert info["provider"].calls == []  # provider_state_current
+    assert "alpha" not in stubs and _Cache.made[0]["alpha"].tolist() == [3.0] * 6
+    assert _Cache.made[0]["rank"] == 4 and _Cache.made[0]["root"].shape == (4, 6)
+    assert out["alpha_cache_used"] and out["love_root_cache_used"]
+    assert "cached_alpha" not in out and "cached_lanczos_root" not in out
+    assert out["provider_state_update_skipped"]
+
+
+def test_exact_and_mean_only_routes(stubs):
+    out = engine.predict(_info(), np.zeros(6), np.zeros((4, 2)), [1.0, 1.0], 0.1, 0.0, 2, 120,
+                         5e-3, 15, 0, False, 64)
+    assert stubs["exact"] == (120, 5e-3, 15, 64)
+    assert _Cache.made[0]["rank"] == 0
+    assert out["variance"].tolist() == [0.5] * 4 and out["exact_cg_total_iterations"] == 11
+    assert "cached_lanczos_root" not in out
+    out = engine.predict(_info(), np.zeros(6), np.zeros((4, 2)), [1.0, 1.0], 0.1, 0.0, 0)
+    assert out["variance"].tolist() == [0.0] * 4 and out["std"].tolist() == [0.0] * 4
+    with pytest.raises(ValueError):
+        engine.predict(_info(), np.zeros(6), np.zeros((1, 2)), [1.0, 1.0], 0.1, 0.0, 3)
+
+
+def test_love_rank_default_for_ard(stubs):
+    info = _info(ard=True)
+    info["provider"].n = 1000
+    engine.predict(info, np.zeros(1000), np.zeros((1, 2)), [1.0] * 3, 0.1, 0.0, 1)
+    assert _Cache.made[0]["rank"] == 200

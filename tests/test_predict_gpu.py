@@ -117,3 +117,28 @@ def test_gp_predict_exact_route(gpb_lib):
     np.testing.assert_allclose(v_e, v_l, rtol=2e-2, atol=1e-4)
     with pytest.raises(ValueError):
         gp.predict(Xs, variance_method="bogus")
+
+
+def test_engine_predict_matches_model_predict(gpb_lib):
+    """engine.predict (the reference binding's call shape and keys) gives the
+    model API's LOVE prediction, and replays it bit for bit from the alpha and
+    root it hands back."""
+    from mojogp_b200 import engine, synthetic
+    from mojogp_b200.gp import SingleOutputGP
+    X, y, Xs = synthetic.config1()
+    X, y = X[::4], y[::4]
+    gp = SingleOutputGP(RBF())
+    tr = gp.fit(X, y, max_iterations=5, method="matrix_free")
+    m_ref, v_ref = gp.predict(Xs, return_var=True, max_root_decomposition_size=100,
+                              max_cg_iterations=300, cg_tolerance=1e-3)
+    info = {"provider": gp._provider, "n": X.shape[0], "is_ard": False}
+    out = engine.predict(info, y, Xs, tr.params, tr.noise, tr.mean, engine.PREDICT_LOVE, 300,
+                         1e-3, 10, 100)
+    np.testing.assert_allclose(out["mean"], m_ref, rtol=1e-5, atol=1e-5)
+    np.testing.assert_allclose(out["variance"], v_ref, rtol=1e-4, atol=1e-6)
+    assert out["cached_lanczos_root"].shape == (100 * X.shape[0],)
+    again = engine.predict(info, y, Xs, tr.params, tr.noise, tr.mean, engine.PREDICT_LOVE, 300,
+                           1e-3, 10, 100, True, 0, out["cached_alpha"], out["cached_lanczos_root"])
+    assert again["alpha_cache_used"] and again["love_root_cache_used"]
+    np.testing.assert_array_equal(again["mean"], out["mean"])
+    np.testing.assert_array_equal(again["variance"], out["variance"])
