@@ -115,6 +115,64 @@ def train(provider: Provider, y: np.ndarray, *, max_iterations: int = 100,
     }
 
 
+def train_binding(info, y, params, noise, max_iterations=100, learning_rate=0.01, num_probes=10,
+                  max_cg_iter=100, cg_tol=1e-2, precond_rank=10, verbose=False,
+                  use_cosine_lr=True, use_preconditioner=True, max_tridiag_iter=30,
+                  precond_rebuild_threshold=0.5, precond_method=0, init_mean=0.0,
+                  enable_early_stopping=False, early_stop_patience=10, early_stop_tol=1e-4,
+                  learn_noise=True, noise_floor=1e-6, noise_regularization=0.01,
+                  progress_callback=None, progress_interval=1, *, trainable_mask=None,
+                  comm=None) -> dict:
+    """The reference engine's `train` with its positional argument order
+    (train_python, jit_engine_bindings.mojo:123-247) and result keys (336-432),
+    over `train` above: the provider takes `params` and `noise` first. Only the
+    greedy pivoted Cholesky (precond_method 0) and the homoskedastic learned
+    noise with the reference's default floor / regularisation are built; a
+    progress callback is not supported (training runs as one device call)."""
+    if int(precond_method) != 0:
+        raise NotImplementedError(
+            f"precond_method={precond_method}: only the greedy pivoted Cholesky (0) is built")
+    if float(noise_floor) != 1e-6 or float(noise_regularization) != 0.01:
+        raise NotImplementedError("noise_floor / noise_regularization other than the defaults "
+                                  "belong to the learned-noise models, which are not built")
+    if progress_callback is not None:
+        raise NotImplementedError("progress callbacks are not supported")
+    prov = info["provider"] if isinstance(info, dict) else info
+    prov.update_params(np.asarray(params, dtype=np.float32))
+    prov.update_noise(float(noise))
+    res = train(prov, y, max_iterations=int(max_iterations), learning_rate=float(learning_rate),
+                num_probes=int(num_probes), max_cg_iter=int(max_cg_iter), cg_tol=float(cg_tol),
+                precond_rank=int(precond_rank), max_tridiag_iter=int(max_tridiag_iter),
+                precond_rebuild_threshold=float(precond_rebuild_threshold),
+                use_cosine_lr=bool(use_cosine_lr), use_preconditioner=bool(use_preconditioner),
+                learn_noise=bool(learn_noise), init_mean=float(init_mean),
+                enable_early_stopping=bool(enable_early_stopping),
+                early_stop_patience=int(early_stop_patience), early_stop_tol=float(early_stop_tol),
+                verbose=bool(verbose), trainable_mask=trainable_mask, comm=comm)
+    mode = int(info.get("materialization_mode", 0)) if isinstance(info, dict) else 0
+    res.update({
+        "training_route": "materialized" if mode == 1 else "matrix_free",
+        "materialization_mode": mode,
+        "is_ard": bool(info.get("is_ard", False)) if isinstance(info, dict) else False,
+        "noise_mode": "scalar",
+        "learn_noise": bool(learn_noise),
+        "noise_floor": float(noise_floor),
+        "noise_regularization": float(noise_regularization),
+        "use_preconditioner": bool(use_preconditioner),
+        "precond_method": int(precond_method),
+        "max_tridiag_iter": int(max_tridiag_iter),
+        "precond_rebuild_threshold": float(precond_rebuild_threshold),
+        "enable_early_stopping": bool(enable_early_stopping),
+        "early_stop_patience": int(early_stop_patience),
+        "early_stop_tol": float(early_stop_tol),
+        "precond_rank": int(precond_rank),
+        "actual_precond_rank": int(res["precond_rank"]),
+        "precond_rebuild_count": max(0, int(res["precond_build_count"]) - 1),
+        "precond_build_total_ms": float(res["precond_build_time_ms"]),
+    })
+    return res
+
+
 def bbmm(provider: Provider, y_centered: np.ndarray, *, num_probes: int = 10,
          max_cg_iter: int = 100, max_tridiag_iter: int = 30, cg_tol: float = 1e-2,
          precond_rank: int = 0, iteration: int = 0, comm=None) -> dict:

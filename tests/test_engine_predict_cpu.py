@@ -120,3 +120,41 @@ def test_love_rank_default_for_ard(stubs):
     info["provider"].n = 1000
     engine.predict(info, np.zeros(1000), np.zeros((1, 2)), [1.0] * 3, 0.1, 0.0, 1)
     assert _Cache.made[0]["rank"] == 200
+
+
+def test_train_binding_maps_the_reference_positional_arguments(monkeypatch):
+    """engine.train_binding takes the reference engine's positional layout
+    (jit_engine_bindings.mojo:123-247) and forwards it to engine.train."""
+    seen = {}
+
+    def fake_train(provider, y, **kw):
+        seen.update(kw)
+        return {"final_nll": 0.5, "noise": 0.1, "mean": 0.0, "iterations": 3, "converged": False,
+                "params": np.ones(2, np.float32), "iter_times_ms": np.ones(3),
+                "nll_history": np.ones(3), "cg_iterations_history": np.ones(3, np.int32),
+                "cached_alpha": None, "precond_build_count": 2, "precond_build_time_ms": 4.0,
+                "precond_rank": 12}
+
+    monkeypatch.setattr(engine, "train", fake_train)
+    info = {"provider": _Prov(), "materialization_mode": 1, "is_ard": True}
+    args = (info, np.zeros(6), np.array([0.7, 1.3]), 0.2, 40, 0.05, 15, 120, 1e-3, 12, False,
+            False, True, 25, 0.4, 0, 0.3, True, 7, 1e-5, False)
+    out = engine.train_binding(*args)
+    assert info["provider"].calls == [("params", [pytest.approx(0.7), pytest.approx(1.3)]),
+                                      ("noise", 0.2)]
+    assert seen == {"max_iterations": 40, "learning_rate": 0.05, "num_probes": 15,
+                    "max_cg_iter": 120, "cg_tol": 1e-3, "precond_rank": 12,
+                    "max_tridiag_iter": 25, "precond_rebuild_threshold": 0.4,
+                    "use_cosine_lr": False, "use_preconditioner": True, "learn_noise": False,
+                    "init_mean": 0.3, "enable_early_stopping": True, "early_stop_patience": 7,
+                    "early_stop_tol": 1e-5, "verbose": False, "trainable_mask": None,
+                    "comm": None}
+    assert out["training_route"] == "materialized" and out["precond_rebuild_count"] == 1
+    assert out["actual_precond_rank"] == 12 and out["precond_build_total_ms"] == 4.0
+    for k in ("final_nll", "noise", "mean", "iterations", "converged", "params", "iter_times_ms",
+              "nll_history", "cg_iterations_history", "cached_alpha", "use_preconditioner",
+              "precond_method", "learn_noise", "is_ard"):
+        assert k in out
+    with pytest.raises(NotImplementedError):
+        engine.train_binding(info, np.zeros(6), [1.0, 1.0], 0.1, 5, 0.01, 10, 100, 1e-2, 10,
+                             False, False, True, 30, 0.5, 2, 0.0)
