@@ -191,40 +191,29 @@ def bbmm(provider: Provider, y_centered: np.ndarray, *, num_probes: int = 10,
 
 PREDICT_MEAN_ONLY, PREDICT_LOVE, PREDICT_EXACT = 0, 1, 2
 _DEFAULT_LOVE_RANK, _DEFAULT_ARD_LOVE_RANK = 100, 200
+_CACHES: dict = {}  # live prediction caches by handle (prepare / predict_with_cache / destroy)
 
 
-def predict(info, y, x_test, params, final_noise: float, final_mean: float,
-            variance_method: int, max_cg_iter: int = 100, cg_tol: float = 1e-2,
-            precond_rank: int = 10, lanczos_rank: int = 0, provider_state_current: bool = False,
-            exact_block_cols: int = 0, cached_alpha=None, cached_love_root=None, test_info=None,
-            *, comm=None) -> dict:
-    """Engine-level prediction with the reference binding's positional arguments
-    and result keys (predict, jit_engine_bindings.mojo:944-1234).
+def _provider_of(info):
+    return info["provider"] if isinstance(info, dict) else info
 
-    Unless `provider_state_current`, the provider takes `params` and
-    `final_noise` first. alpha = (K + noise I)^{-1} (y - final_mean) by CG
-    (`max_cg_iter`, `cg_tol`), or `cached_alpha`. variance_method 0: mean only;
-    1: LOVE with a root of `lanczos_rank` vectors (<= 0: 100, 200 for ARD
-    kernels; _resolve_exact_predict_lanczos_rank,
-    jit_engine_binding_helpers.mojo:23-45), or `cached_love_root` [rank * n];
-    2: CG-exact variance (blocks of `exact_block_cols`, preconditioner rank
-    `precond_rank`). Variances include the noise. The result carries
-    `cached_alpha` / `cached_lanczos_root` when they were computed here, for the
-    caller to pass back. `test_info` is accepted for signature compatibility:
-    test-point diagonals come from the training provider's kernel.
-    """
+
+def _check_variance_method(variance_method) -> None:
+    if variance_method not in (PREDICT_MEAN_ONLY, PREDICT_LOVE, PREDICT_EXACT):
+        raise ValueError(f"variance_method must be 0, 1 or 2, got {variance_method}")
+
+
+def _build_cache(info, y, params, final_noise, final_mean, variance_method, max_cg_iter, cg_tol,
+                 lanczos_rank, provider_state_current, cached_alpha, cached_love_root, comm):
+    """Provider update, alpha (CG or cached) and the LOVE root (Lanczos or
+    cached) in a device prediction cache; returns (cache, alpha, facts)."""
     import time
 
     from . import prediction
 
-    if variance_method not in (PREDICT_MEAN_ONLY, PREDICT_LOVE, PREDICT_EXACT):
-        raise ValueError(f"variance_method must be 0, 1 or 2, got {variance_method}")
-    prov = info["provider"] if isinstance(info, dict) else info
+    _check_variance_method(variance_method)
+    prov = _provider_of(info)
     n = prov.n
-    Xt = np.ascontiguousarray(x_test, dtype=np.float32)
-    if Xt.ndim == 1:
-        Xt = Xt[:, None]
-    t_start = time.perf_counter()
     if not provider_state_current:
         prov.update_params(np.asarray(params, dtype=np.float32))
         prov.update_noise(float(final_noise))
@@ -240,6 +229,7 @@ def predict(info, y, x_test, params, final_noise: float, final_mean: float,
     alpha_s = time.perf_counter() - t0
     rank, root, root_cached = 0, None, False
     if variance_method == PREDICT_LOVE:
+        # _resolve_exact_predict_lanczos_rank (jit_engine_binding_helpers.mojo:23-45)
         is_ard = bool(info.get("is_ard", False)) if isinstance(info, dict) else False
         rank = lanczos_rank if lanczos_rank > 0 else (
             _DEFAULT_ARD_LOVE_RANK if is_ard else _DEFAULT_LOVE_RANK)
@@ -251,40 +241,140 @@ def predict(info, y, x_test, params, final_noise: float, final_mean: float,
     t1 = time.perf_counter()
     cache = prediction.PredictionCache(prov, alpha, float(final_mean), rank, root=root, comm=comm)
     root_s = time.perf_counter() - t1 if (rank > 0 and not root_cached) else 0.0
-    try:
-        t2 = time.perf_counter()
-        mean, var = cache.predict(Xt, return_var=variance_method == PREDICT_LOVE)
-        mean_s = time.perf_counter() - t2
-        exact_iters = 0
-        var_s = 0.0  # LOVE: the variance comes out of the same cross-product pass as the mean
-        if variance_method == PREDICT_EXACT:
-            t3 = time.perf_counter()
-            var, exact_iters = prediction.exact_variance(prov, Xt, max_cg_iter, cg_tol,
-                                                         precond_rank, exact_block_cols,
-                                                         comm=comm)
-            var_s = time.perf_counter() - t3
-        root_out = cache.root() if (variance_method == PREDICT_LOVE and not root_cached) else None
-    finally:
-        cache.destroy()
+    facts = {"alpha_time_s": alpha_s, "love_root_time_s": root_s,
+             "alpha_cache_used": alpha_cache_used, "love_root_cache_used": root_cached,
+             "rank": rank}
+    return cache, alpha, facts
+
+
+def _predict_from_cache(info, cache, x_test, params, final_noise, variance_method, max_cg_iter,
+                        cg_tol, precond_rank, provider_state_current, exact_block_cols, comm):
+    import time
+
+    from . import prediction
+
+    _check_variance_method(variance_method)
+    prov = _provider_of(info)
+    if not provider_state_current:
+        prov.update_params(np.asarray(params, dtype=np.float32))
+        prov.update_noise(float(final_noise))
+    Xt = np.ascontiguousarray(x_test, dtype=np.float32)
+    if Xt.ndim == 1:
+        Xt = Xt[:, None]
+    t2 = time.perf_counter()
+    mean, var = cache.predict(Xt, return_var=variance_method == PREDICT_LOVE)
+    mean_s = time.perf_counter() - t2
+    exact_iters, var_s = 0, 0.0  # LOVE: the variance comes out of the mean's cross-product pass
+    if variance_method == PREDICT_EXACT:
+        t3 = time.perf_counter()
+        var, exact_iters = prediction.exact_variance(prov, Xt, max_cg_iter, cg_tol, precond_rank,
+                                                     exact_block_cols, comm=comm)
+        var_s = time.perf_counter() - t3
     m = Xt.shape[0]
-    if var is None:
-        var = np.zeros(m, np.float32)
-    var = np.asarray(var, dtype=np.float32)
-    out = {
+    var = np.zeros(m, np.float32) if var is None else np.asarray(var, dtype=np.float32)
+    return {
         "mean": np.asarray(mean, dtype=np.float32),
         "variance": var,
         "std": np.sqrt(np.maximum(var, 0)).astype(np.float32),
-        "alpha_time_s": alpha_s,
         "mean_time_s": mean_s,
         "variance_time_s": var_s,
-        "love_root_time_s": root_s,
-        "total_time_s": time.perf_counter() - t_start,
         "exact_cg_total_iterations": int(exact_iters),
         "provider_state_update_skipped": bool(provider_state_current),
-        "alpha_cache_used": alpha_cache_used,
-        "love_root_cache_used": root_cached,
     }
-    if not alpha_cache_used:
+
+
+def prepare_prediction_cache(info, y, params, final_noise: float, final_mean: float,
+                             variance_method: int, max_cg_iter: int = 100, cg_tol: float = 1e-2,
+                             precond_rank: int = 10, lanczos_rank: int = 0,
+                             provider_state_current: bool = False, cached_alpha=None,
+                             cached_love_root=None, *, comm=None) -> dict:
+    """Device-resident alpha and LOVE root for repeated predictions, with the
+    reference binding's positional arguments and result keys
+    (prepare_prediction_cache, jit_engine_bindings.mojo:636-768). The returned
+    `cache_handle` goes to predict_with_cache / destroy_prediction_cache."""
+    import time
+
+    t = time.perf_counter()
+    cache, _, f = _build_cache(info, y, params, final_noise, final_mean, variance_method,
+                               max_cg_iter, cg_tol, lanczos_rank, provider_state_current,
+                               cached_alpha, cached_love_root, comm)
+    handle = int(cache.handle)
+    _CACHES[handle] = cache
+    return {"cache_handle": handle, "n_train": int(_provider_of(info).n), "rank": f["rank"],
+            "has_love_root": f["rank"] > 0, "alpha_time_s": f["alpha_time_s"],
+            "love_root_time_s": f["love_root_time_s"], "prepare_time_s": time.perf_counter() - t,
+            "alpha_cache_used": f["alpha_cache_used"],
+            "love_root_cache_used": f["love_root_cache_used"]}
+
+
+def predict_with_cache(info, cache_handle: int, x_test, params, final_noise: float,
+                       final_mean: float, variance_method: int, max_cg_iter: int = 100,
+                       cg_tol: float = 1e-2, precond_rank: int = 10, lanczos_rank: int = 0,
+                       provider_state_current: bool = False, exact_block_cols: int = 0,
+                       test_info=None, *, comm=None) -> dict:
+    """Prediction from a prepared cache (predict_with_cache,
+    jit_engine_bindings.mojo:782-942): mean from the cached alpha, LOVE variance
+    from the cached root, CG-exact variance on demand."""
+    import time
+
+    cache = _CACHES.get(int(cache_handle)) if cache_handle else None
+    if cache is None:
+        raise ValueError("predict_with_cache() received null or unknown cache handle")
+    t = time.perf_counter()
+    out = _predict_from_cache(info, cache, x_test, params, final_noise, variance_method,
+                              max_cg_iter, cg_tol, precond_rank, provider_state_current,
+                              exact_block_cols, comm)
+    out.update({"alpha_time_s": 0.0, "love_root_time_s": 0.0,
+                "total_time_s": time.perf_counter() - t, "alpha_cache_used": True,
+                "love_root_cache_used": variance_method == PREDICT_LOVE and cache.rank > 0,
+                "prediction_cache_used": True})
+    return out
+
+
+def destroy_prediction_cache(cache_handle: int) -> None:
+    """Release a cache from prepare_prediction_cache (jit_engine_bindings.mojo:770-780)."""
+    cache = _CACHES.pop(int(cache_handle), None)
+    if cache is not None:
+        cache.destroy()
+
+
+def predict(info, y, x_test, params, final_noise: float, final_mean: float,
+            variance_method: int, max_cg_iter: int = 100, cg_tol: float = 1e-2,
+            precond_rank: int = 10, lanczos_rank: int = 0, provider_state_current: bool = False,
+            exact_block_cols: int = 0, cached_alpha=None, cached_love_root=None, test_info=None,
+            *, comm=None) -> dict:
+    """Engine-level prediction with the reference binding's positional arguments
+    and result keys (predict, jit_engine_bindings.mojo:944-1234).
+
+    Unless `provider_state_current`, the provider takes `params` and
+    `final_noise` first. alpha = (K + noise I)^{-1} (y - final_mean) by CG
+    (`max_cg_iter`, `cg_tol`), or `cached_alpha`. variance_method 0: mean only;
+    1: LOVE with a root of `lanczos_rank` vectors (<= 0: 100, 200 for ARD
+    kernels), or `cached_love_root` [rank * n]; 2: CG-exact variance (blocks of
+    `exact_block_cols`, preconditioner rank `precond_rank`). Variances include
+    the noise. The result carries `cached_alpha` / `cached_lanczos_root` when
+    they were computed here, for the caller to pass back. `test_info` is
+    accepted for signature compatibility: test-point diagonals come from the
+    training provider's kernel.
+    """
+    import time
+
+    t_start = time.perf_counter()
+    cache, alpha, f = _build_cache(info, y, params, final_noise, final_mean, variance_method,
+                                   max_cg_iter, cg_tol, lanczos_rank, provider_state_current,
+                                   cached_alpha, cached_love_root, comm)
+    try:
+        out = _predict_from_cache(info, cache, x_test, params, final_noise, variance_method,
+                                  max_cg_iter, cg_tol, precond_rank, True, exact_block_cols, comm)
+        root_out = cache.root() if (f["rank"] > 0 and not f["love_root_cache_used"]) else None
+    finally:
+        cache.destroy()
+    out.update({"alpha_time_s": f["alpha_time_s"], "love_root_time_s": f["love_root_time_s"],
+                "total_time_s": time.perf_counter() - t_start,
+                "provider_state_update_skipped": bool(provider_state_current),
+                "alpha_cache_used": f["alpha_cache_used"],
+                "love_root_cache_used": f["love_root_cache_used"]})
+    if not f["alpha_cache_used"]:
         out["cached_alpha"] = alpha
     if root_out is not None:
         out["cached_lanczos_root"] = root_out.ravel()

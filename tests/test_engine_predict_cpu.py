@@ -30,6 +30,7 @@ class _Cache:
         _Cache.made.append(dict(alpha=np.asarray(alpha), mean=mean, rank=love_rank, root=root))
         self.rank, self.n = love_rank, provider.n
         self.destroyed = False
+        self.handle = id(self)
 
     def predict(self, Xt, return_var=True):
         m = Xt.shape[0]
@@ -158,3 +159,28 @@ def test_train_binding_maps_the_reference_positional_arguments(monkeypatch):
     with pytest.raises(NotImplementedError):
         engine.train_binding(info, np.zeros(6), [1.0, 1.0], 0.1, 5, 0.01, 10, 100, 1e-2, 10,
                              False, False, True, 30, 0.5, 2, 0.0)
+
+
+def test_prepared_cache_round_trip(stubs):
+    """prepare_prediction_cache -> predict_with_cache (several times) ->
+    destroy_prediction_cache, with the reference bindings' keys."""
+    info = _info()
+    prep = engine.prepare_prediction_cache(info, np.ones(6), [1.0, 1.0], 0.1, 1.0, 1, 80, 1e-3,
+                                           10, 3, False)
+    assert prep["rank"] == 3 and prep["has_love_root"] and prep["n_train"] == 6
+    assert not prep["alpha_cache_used"] and stubs["alpha"][1:] == (80, 1e-3)
+    h = prep["cache_handle"]
+    for _ in range(2):
+        out = engine.predict_with_cache(info, h, np.zeros((5, 2)), [1.0, 1.0], 0.1, 1.0, 1,
+                                        provider_state_current=True)
+        assert out["variance"].tolist() == [0.25] * 5 and out["prediction_cache_used"]
+        assert out["love_root_cache_used"] and out["alpha_cache_used"]
+    out = engine.predict_with_cache(info, h, np.zeros((2, 2)), [1.0, 1.0], 0.1, 1.0, 2, 90, 1e-4,
+                                    5, 0, True, 32)
+    assert stubs["exact"] == (90, 1e-4, 5, 32) and out["variance"].tolist() == [0.5, 0.5]
+    cache = engine._CACHES[h]
+    engine.destroy_prediction_cache(h)
+    assert cache.destroyed and h not in engine._CACHES
+    with pytest.raises(ValueError, match="cache handle"):
+        engine.predict_with_cache(info, h, np.zeros((1, 2)), [1.0, 1.0], 0.1, 1.0, 1)
+    engine.destroy_prediction_cache(h)  # a second destroy is harmless
