@@ -515,3 +515,13 @@ def fit_gp(X, y, kernel: KernelNode, **kw) -> SingleOutputGP:
     gp = SingleOutputGP(kernel)
     gp.fit(X, y, **kw)
     return gp
+
+
+def fit_gp(X: np.ndarray, y: np.ndarray, kernel: Optional[KernelNode] = None,
+           **kwargs) -> SingleOutputGP:
+    """Create and fit a SingleOutputGP in one call (fit_gp, gp.py:3928-3949);
+    the kernel defaults to RBF and the keyword arguments go to fit()."""
+    from .kernel import Kernel
+    gp = SingleOutputGP(kernel if kernel is not None else Kernel.rbf())
+    gp.fit(X, y, **kwargs)
+    return gp

@@ -16,7 +16,7 @@ parameters (kernel.py:553-556).
 from __future__ import annotations
 
 import copy
-from dataclasses import dataclass, field
+from dataclasses import dataclass
 from enum import Enum
 from typing import Dict, List, Optional, Sequence, Union
 

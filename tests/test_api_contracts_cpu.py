@@ -142,3 +142,36 @@ def test_fit_route_defaults_follow_the_reference():
     assert _route("matrix_free", 20000, 4, K.MATERN52)["precond_rank"] == 0
     assert _route("matrix_free", 20000, 4, K.MATERN52, preconditioner="greedy")["precond_rank"] is None
     assert _route("matrix_free", 20000, 4, K.RBF, use_preconditioner=False)["precond_rank"] is None
+
+
+def test_standard_scaler_round_trip():
+    from mojogp_b200 import StandardScaler
+    rng = np.random.default_rng(3)
+    X = rng.normal(5.0, 3.0, size=(200, 3))
+    X[:, 2] = 7.0  # constant feature keeps scale 1
+    y = rng.normal(-2.0, 0.5, size=200)
+    sc = StandardScaler()
+    Xs, ys = sc.fit_transform(X, y)
+    assert Xs.dtype == np.float32 and ys.dtype == np.float32
+    np.testing.assert_allclose(Xs[:, :2].mean(0), 0, atol=1e-5)
+    np.testing.assert_allclose(Xs[:, :2].std(0), 1, atol=1e-5)
+    assert np.all(Xs[:, 2] == 0) and sc.X_std_[2] == 1.0
+    np.testing.assert_allclose(sc.inverse_transform_X(Xs), X, rtol=1e-5, atol=1e-5)
+    m, s = sc.inverse_transform_y(ys, std=np.ones(200))
+    np.testing.assert_allclose(m, y, rtol=1e-5, atol=1e-6)
+    np.testing.assert_allclose(s, y.std(), rtol=1e-6)
+    _, v = sc.inverse_transform_y(ys, variance=np.ones(200))
+    np.testing.assert_allclose(v, y.std() ** 2, rtol=1e-6)
+    assert len(sc.inverse_transform_y(ys)) == 1
+    only_x = StandardScaler()
+    assert len(only_x.fit_transform(X)) == 1
+    with pytest.raises(RuntimeError, match="not fitted with y"):
+        only_x.transform_y(y)
+    with pytest.raises(RuntimeError, match="fit"):
+        StandardScaler().transform_X(X)
+
+
+def test_fit_gp_validates_before_device_work():
+    from mojogp_b200 import RBF, fit_gp
+    with pytest.raises(ValueError, match="max_iterations must be > 0"):
+        fit_gp(np.zeros((4, 2), np.float32), np.zeros(4, np.float32), RBF(), max_iterations=0)
