@@ -17,6 +17,7 @@ from __future__ import annotations
 
 import ctypes as C
 import math
+from dataclasses import dataclass
 from typing import List, Optional
 
 import numpy as np
@@ -41,6 +42,30 @@ def _isp(y):
 
 def _dsp(x):
     return 1.0 / (1.0 + math.exp(-x)) if x > -20 else math.exp(x)
+
+
+@dataclass
+class MultiOutputPredictionResult:
+    """Multi-output prediction (MultiOutputPredictionResult,
+    multi_output_gp.py:545-550): mean [m, T], variance and std [m, T] or None."""
+
+    mean: np.ndarray
+    variance: Optional[np.ndarray] = None
+    std: Optional[np.ndarray] = None
+
+
+def _prediction_output(mean, var, return_var: bool, return_std: bool):
+    """The multi-output predict return convention: (mean, std) with return_std,
+    (mean, variance) with return_var (zeros when no variance was computed),
+    otherwise a MultiOutputPredictionResult."""
+    if not (return_var or return_std):
+        return MultiOutputPredictionResult(
+            mean=mean, variance=var, std=None if var is None else np.sqrt(np.maximum(var, 0)))
+    if var is None:
+        var = np.zeros_like(mean)
+    if return_std:
+        return mean, np.sqrt(np.maximum(var, 0))
+    return mean, var
 
 
 def build_lmc_initial_params_from_lengthscales(kernels, initial_lengthscales) -> np.ndarray:
@@ -416,23 +441,25 @@ class MultiOutputLMCGP:
         if Xt.ndim == 1 and self.dim == 1:
             Xt = Xt[:, None]
         _check_test_inputs(Xt, self.dim)
+        mean = self._predict_mean(Xt)
+        var = None if variance_method == "mean_only" else self._predict_var(Xt, variance_method)
+        return _prediction_output(mean, var, return_var, return_std)
+
+    def _predict_mean(self, Xt: np.ndarray) -> np.ndarray:
         T, n = self.T, self._X.shape[0]
         alpha = self._alpha.reshape(T, n).T  # [n, T]
         mean = np.zeros((Xt.shape[0], T))
         for s, prov in enumerate(self._lmc.providers):
             Cs = prov.cross_matvec_host(Xt, alpha)  # [n*, T] = K_s(X*, X) alpha_j
             mean += Cs @ self.A[s].T
-        mean = (mean + self.mean_[None, :]).astype(np.float32)
-        if not (return_var or return_std):
-            return mean
-        if variance_method == "mean_only":
-            return mean, np.zeros_like(mean)
+        return (mean + self.mean_[None, :]).astype(np.float32)
+
+    def _predict_var(self, Xt: np.ndarray, variance_method: str) -> np.ndarray:
+        T, n = self.T, self._X.shape[0]
         if variance_method == "exact":
             tol = min(float(self.cg_tol), 1e-2) if self.cg_tol > 0 else 1e-2
             var, _ = self._lmc.exact_variance(Xt, max(int(self.max_cg_iter), 100), tol)
-            if return_std:
-                return mean, np.sqrt(var)
-            return mean, var
+            return var
         from .gp import _DEFAULT_PREDICT_LANCZOS_RANK
         from .prediction import PredictionCache
         avg_noise = float(np.mean(self.noise))
@@ -453,10 +480,7 @@ class MultiOutputLMCGP:
             latent = np.maximum(v_s.astype(np.float64) - avg_noise, 1e-10)
             row_w = (self.A[s] ** 2).sum(axis=1)  # sum_t' A_s[t][t']^2
             var += latent[:, None] * row_w[None, :]
-        var = (var + self.noise[None, :]).astype(np.float32)
-        if return_std:
-            return mean, np.sqrt(var)
-        return mean, var
+        return (var + self.noise[None, :]).astype(np.float32)
 
 
 def _icm_initial_W(T: int, R: int, seed: int = 42) -> np.ndarray:
@@ -700,8 +724,8 @@ class MultiOutputGP:
         alpha = self._alpha.reshape(T, n).T
         Cs = prov.cross_matvec_host(Xt, alpha)  # [m, T]
         mean = (Cs @ self.task_covariance.T + self.mean_[None, :]).astype(np.float32)
-        if not (return_var or return_std) or variance_method == "mean_only":
-            return mean if not (return_var or return_std) else (mean, np.zeros_like(mean))
+        if variance_method == "mean_only":
+            return _prediction_output(mean, None, return_var, return_std)
         from .gp import _DEFAULT_PREDICT_LANCZOS_RANK
         from .prediction import PredictionCache, exact_variance
         s2 = float(np.mean(self.noise_per_task))
@@ -728,6 +752,4 @@ class MultiOutputGP:
         finally:
             prov.update_noise(0.0)
         var = np.maximum(var, 0).astype(np.float32)
-        if return_std:
-            return mean, np.sqrt(var)
-        return mean, var
+        return _prediction_output(mean, var, return_var, return_std)

@@ -175,3 +175,21 @@ def test_fit_gp_validates_before_device_work():
     from mojogp_b200 import RBF, fit_gp
     with pytest.raises(ValueError, match="max_iterations must be > 0"):
         fit_gp(np.zeros((4, 2), np.float32), np.zeros(4, np.float32), RBF(), max_iterations=0)
+
+
+def test_multi_output_prediction_return_convention():
+    """No flags: a MultiOutputPredictionResult (multi_output_gp.py:545-550);
+    return_std / return_var: tuples; mean-only variance is zeros in a tuple and
+    None in the result object."""
+    from mojogp_b200.multi_output_gp import MultiOutputPredictionResult, _prediction_output
+    mean = np.ones((3, 2), np.float32)
+    var = np.full((3, 2), 4.0, np.float32)
+    r = _prediction_output(mean, var, False, False)
+    assert isinstance(r, MultiOutputPredictionResult)
+    assert np.all(r.std == 2.0) and r.variance is var and r.mean is mean
+    assert _prediction_output(mean, var, True, False)[1] is var
+    assert np.all(_prediction_output(mean, var, False, True)[1] == 2.0)
+    assert np.all(_prediction_output(mean, var, True, True)[1] == 2.0)
+    r = _prediction_output(mean, None, False, False)
+    assert r.variance is None and r.std is None
+    assert np.all(_prediction_output(mean, None, True, False)[1] == 0)

@@ -33,7 +33,9 @@ def test_icm_fit_predict(gpb_lib):
     gp.fit(X, Y, max_iterations=25, learning_rate=0.05)
     h = gp.nll_history
     assert np.all(np.isfinite(h)) and h.min() < h[0]
-    mean = gp.predict(X[:200])
+    pred = gp.predict(X[:200])  # no flags: a MultiOutputPredictionResult, as the reference
+    mean = pred.mean
+    assert pred.variance.shape == (200, 3) and np.all(np.isfinite(pred.std))
     r2 = 1 - np.mean((mean - Y[:200]) ** 2) / np.var(Y[:200])
     assert mean.shape == (200, 3) and r2 > 0.9
     B = gp.task_covariance

@@ -70,9 +70,12 @@ def test_lmc_fit_predict_config4_small(gpb_lib):
     gp.fit(X, Y, max_iterations=15, learning_rate=0.05)
     h = gp.nll_history
     assert np.all(np.isfinite(h)) and h[-1] < h[0]
-    mean = gp.predict(X[:500])
+    pred = gp.predict(X[:500])  # no flags: a MultiOutputPredictionResult, as the reference
+    mean = pred.mean
     r2 = 1 - np.mean((mean - Y[:500]) ** 2) / np.var(Y[:500])
     assert mean.shape == (500, 4) and r2 > 0.8
+    assert pred.variance.shape == (500, 4) and np.all(pred.variance > 0)
+    np.testing.assert_allclose(pred.std, np.sqrt(pred.variance), rtol=1e-6)
 
 
 def _ill_conditioned(n=150, d=2, T=3, seed=5):
