@@ -54,6 +54,12 @@ class MultiOutputPredictionResult:
     std: Optional[np.ndarray] = None
 
 
+def _named(kernel, params, pick) -> np.ndarray:
+    """The entries of `params` whose names (kernel.get_param_names) satisfy `pick`."""
+    names = kernel.get_param_names()
+    return np.asarray([float(params[i]) for i, nm in enumerate(names) if pick(nm)], np.float32)
+
+
 def _prediction_output(mean, var, return_var: bool, return_std: bool):
     """The multi-output predict return convention: (mean, std) with return_std,
     (mean, variance) with return_var (zeros when no variance was computed),
@@ -420,6 +426,68 @@ class MultiOutputLMCGP:
         self._alpha, _ = self._lmc.solve(yc, 300, 1e-3)
         return self
 
+    # Training-result fields (LMCTrainingResult, multi_output_gp.py:3405-3464): fit()
+    # returns the model, which answers for the result object.
+    @property
+    def num_tasks(self) -> int:
+        return self.T
+
+    @property
+    def iterations(self) -> int:
+        return len(self.nll_history)
+
+    @property
+    def converged(self) -> bool:
+        return False  # the LMC loop runs its iteration budget
+
+    @property
+    def noise_per_task(self) -> np.ndarray:
+        return np.asarray(self.noise)
+
+    @property
+    def params_per_latent(self) -> list:
+        return [np.asarray(p) for p in self.params_]
+
+    @property
+    def A_matrices(self) -> np.ndarray:
+        return np.asarray(self.A)
+
+    @property
+    def B(self) -> np.ndarray:
+        return np.asarray(self.A).sum(axis=0)
+
+    @property
+    def Lambda(self) -> np.ndarray:
+        return np.linalg.eigh(self.B)[0]
+
+    @property
+    def Q(self) -> np.ndarray:
+        return np.linalg.eigh(self.B)[1]
+
+    @property
+    def alpha(self) -> np.ndarray:
+        """[n, T] solution of K_full alpha = y - mean (task-blocked internally)."""
+        return self._alpha.reshape(self.T, -1).T
+
+    @property
+    def mean_per_task(self) -> np.ndarray:
+        return np.asarray(self.mean_)
+
+    @property
+    def use_ard(self) -> bool:
+        return bool(self.ard)
+
+    @property
+    def lengthscales(self) -> np.ndarray:
+        """Every latent's lengthscale parameters, in latent order."""
+        return np.concatenate([_named(k, p, lambda nm: nm.endswith("_lengthscale") or "_ls_" in nm)
+                               for k, p in zip(self.kernels_resolved, self.params_)])
+
+    @property
+    def outputscales(self) -> np.ndarray:
+        return np.concatenate([_named(k, p, lambda nm: nm.endswith("_outputscale"))
+                               for k, p in zip(self.kernels_resolved, self.params_)])
+
     def log_marginal_likelihood(self) -> float:
         return -float(self.final_nll)
 
@@ -704,6 +772,52 @@ class MultiOutputGP:
         self.final_nll = best_nll
         self.converged = converged
         return self
+
+    # Training-result fields (MultiOutputTrainingResult, multi_output_gp.py:475-543):
+    # fit() returns the model, which answers for the result object.
+    @property
+    def num_tasks(self) -> int:
+        return self.T
+
+    @property
+    def iterations(self) -> int:
+        return len(self.nll_history)
+
+    @property
+    def noise(self) -> float:
+        return float(np.mean(self.noise_per_task))
+
+    @property
+    def params(self) -> np.ndarray:
+        return np.asarray(self.params_)
+
+    @property
+    def num_kernel_params(self) -> int:
+        return int(np.asarray(self.params_).shape[0])
+
+    @property
+    def B(self) -> np.ndarray:
+        return self.task_covariance
+
+    @property
+    def Q(self) -> np.ndarray:
+        return self._Q
+
+    @property
+    def Lambda(self) -> np.ndarray:
+        return self._Lambda
+
+    @property
+    def effective_scales(self) -> np.ndarray:
+        return self._Lambda
+
+    @property
+    def W(self) -> np.ndarray:
+        return self.W_
+
+    @property
+    def mean_per_task(self) -> np.ndarray:
+        return np.asarray(self.mean_)
 
     def log_marginal_likelihood(self) -> float:
         return -float(self.final_nll)

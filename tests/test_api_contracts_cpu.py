@@ -193,3 +193,42 @@ def test_multi_output_prediction_return_convention():
     r = _prediction_output(mean, None, False, False)
     assert r.variance is None and r.std is None
     assert np.all(_prediction_output(mean, None, True, False)[1] == 0)
+
+
+def test_fitted_models_answer_for_the_reference_result_fields():
+    """fit() returns the model; its properties give the reference result
+    objects' fields (LMCTrainingResult, MultiOutputTrainingResult) from the
+    attributes the fit loop sets. Populated here by hand (no device)."""
+    from mojogp_b200.kernel import Matern32, make_ard_kernel
+    lmc = object.__new__(MultiOutputLMCGP)
+    T, n = 2, 5
+    lmc.T, lmc.ard = T, True
+    lmc.kernels_resolved = [make_ard_kernel(RBF(ard=True), 2), Matern32().resolve_ard(2)]
+    lmc.params_ = [np.array([0.5, 0.7, 1.5]), np.array([0.9, 2.0])]
+    lmc.A = np.stack([np.eye(T), 2 * np.eye(T)])
+    lmc.noise = np.array([0.1, 0.2])
+    lmc.mean_ = np.array([1.0, -1.0])
+    lmc.nll_history = np.array([3.0, 2.0, 1.5])
+    lmc._alpha = np.arange(T * n, dtype=np.float32)
+    assert lmc.num_tasks == 2 and lmc.iterations == 3 and lmc.converged is False
+    np.testing.assert_array_equal(lmc.B, 3 * np.eye(T))
+    np.testing.assert_allclose(lmc.Lambda, [3.0, 3.0])
+    assert lmc.alpha.shape == (n, T) and lmc.alpha[1, 1] == n + 1
+    np.testing.assert_allclose(lmc.lengthscales, [0.5, 0.7, 0.9])
+    np.testing.assert_allclose(lmc.outputscales, [1.5, 2.0])
+    np.testing.assert_array_equal(lmc.noise_per_task, [0.1, 0.2])
+    assert lmc.use_ard and len(lmc.params_per_latent) == 2
+    icm = object.__new__(MultiOutputGP)
+    icm.T = 3
+    icm.noise_per_task = np.array([0.1, 0.2, 0.3])
+    icm.params_ = np.array([0.8, 1.0], np.float32)
+    icm.task_covariance = np.diag([1.0, 2.0, 3.0])
+    icm._Q, icm._Lambda = np.eye(3), np.array([1.0, 2.0, 3.0])
+    icm.W_ = np.ones((3, 1))
+    icm.mean_ = np.zeros(3)
+    icm.nll_history = np.array([1.0, 0.5])
+    assert icm.num_tasks == 3 and icm.iterations == 2 and icm.num_kernel_params == 2
+    assert icm.noise == pytest.approx(0.2)
+    np.testing.assert_array_equal(icm.B, icm.task_covariance)
+    np.testing.assert_array_equal(icm.effective_scales, [1.0, 2.0, 3.0])
+    assert icm.W.shape == (3, 1) and icm.params.shape == (2,)
