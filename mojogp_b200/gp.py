@@ -62,6 +62,20 @@ def _check_multi_output_data(X: np.ndarray, Y: np.ndarray) -> None:
     _check_finite("Y", Y)
 
 
+def _checked_observation_noise(noise, m: int, floor: float = 1e-6) -> np.ndarray:
+    """Test-point observation noise for observed prediction (gp.py:2786-2798)."""
+    if noise is None:
+        raise ValueError("predict_observed()/predict(target='observed') requires "
+                         "observation_noise for test points")
+    obs = np.ascontiguousarray(noise, dtype=np.float32)
+    if obs.shape != (m,):
+        raise ValueError(f"observation_noise must have shape ({m},), got {obs.shape}")
+    _check_finite("observation_noise", obs)
+    if np.any(obs < floor):
+        raise ValueError("observation_noise values must be >= noise_floor")
+    return obs
+
+
 def _check_test_inputs(Xt: np.ndarray, dim: int) -> None:
     """Prediction input checks (multi_output_gp.py:2565-2573)."""
     if Xt.ndim != 2:
@@ -384,13 +398,25 @@ class SingleOutputGP:
                 cg_tolerance: Optional[float] = None,
                 max_root_decomposition_size: Optional[int] = None,
                 preconditioner_rank: Optional[int] = None,
-                exact_prediction_block_cols: Optional[int] = None):
-        """Predictive mean and variance / std including the noise term: LOVE
-        (variance_method="love"), CG-exact ("exact") or none ("mean_only")."""
+                exact_prediction_block_cols: Optional[int] = None, target: str = "latent",
+                observation_noise: Optional[np.ndarray] = None):
+        """Predictive mean and variance / std: LOVE (variance_method="love"),
+        CG-exact ("exact") or none ("mean_only"). As the reference's engine does
+        (jit_prediction.mojo:2048-2051), the variance includes the learned noise;
+        target="observed" adds the given test-point `observation_noise` [m] on
+        top (predict / _add_observation_noise_to_prediction, gp.py:2446-2809).
+        Returns (mean, var) with return_var, (mean, std) with return_std,
+        otherwise a PredictionResult."""
         if not self._is_trained:
-            raise RuntimeError("GP must be trained first.")
+            raise RuntimeError("GP must be trained before prediction. Call fit() first.")
+        if return_var and return_std:
+            raise ValueError("Only one of return_var or return_std may be True.")
         if variance_method not in ("love", "exact", "mean_only"):
             raise ValueError("variance_method must be one of 'love', 'exact', 'mean_only'")
+        if target not in ("latent", "observed"):
+            raise ValueError("target must be 'latent' or 'observed'")
+        if exact_prediction_block_cols is not None and exact_prediction_block_cols <= 0:
+            raise ValueError("exact_prediction_block_cols must be positive or None")
         Xt = np.ascontiguousarray(X_test, dtype=np.float32)
         if Xt.ndim == 1 and self.dim == 1:
             Xt = Xt[:, None]
@@ -415,12 +441,60 @@ class SingleOutputGP:
                 block_cols=exact_prediction_block_cols or 0, comm=self._comm)
         if var is None:
             var = np.zeros_like(mean)
+        if target == "observed":
+            var = var + _checked_observation_noise(observation_noise, Xt.shape[0])
         std = np.sqrt(np.maximum(var, 0))
         if return_var:
             return mean, var
         if return_std:
             return mean, std
         return PredictionResult(mean=mean, variance=var, std=std)
+
+    def predict_latent(self, X, **kwargs):
+        """p(f_test | y_train) (predict_latent, gp.py:2676-2679)."""
+        kwargs.pop("target", None)
+        return self.predict(X, target="latent", **kwargs)
+
+    def predict_observed(self, X, observation_noise: Optional[np.ndarray] = None, **kwargs):
+        """p(y_test | y_train) with explicit test-point noise (predict_observed,
+        gp.py:2681-2700): the training noise is never reused for new points."""
+        kwargs.pop("target", None)
+        return self.predict(X, target="observed", observation_noise=observation_noise, **kwargs)
+
+    def score(self, X_test, y_test) -> float:
+        """R^2 of the predictive mean (score, gp.py:3059-3070)."""
+        if not self._is_trained:
+            raise RuntimeError("Model must be trained before scoring")
+        y_test = np.asarray(y_test, dtype=np.float32)
+        mean, _ = self.predict(np.asarray(X_test, dtype=np.float32), return_std=True)
+        ss_res = float(np.sum((y_test - mean) ** 2))
+        ss_tot = float(np.sum((y_test - np.mean(y_test)) ** 2))
+        return 0.0 if ss_tot == 0 else 1.0 - ss_res / ss_tot
+
+    # Reference read-only members (gp.py:740-779).
+    @property
+    def num_params(self) -> int:
+        return (self.kernel or self.kernel_spec).num_params()
+
+    @property
+    def param_names(self) -> list:
+        return (self.kernel or self.kernel_spec).get_param_names()
+
+    @property
+    def is_trained(self) -> bool:
+        return self._is_trained
+
+    @property
+    def training_result(self) -> Optional[TrainingResult]:
+        return self._training_result
+
+    @property
+    def nll_history(self) -> Optional[np.ndarray]:
+        return None if self._training_result is None else self._training_result.nll_history
+
+    @property
+    def backend_train_info(self) -> Optional[dict]:
+        return dict(self._train_info) if self._train_info else None
 
     # ---------------------------------------------------------------- queries
     def log_marginal_likelihood(self) -> float:

@@ -232,3 +232,48 @@ def test_fitted_models_answer_for_the_reference_result_fields():
     np.testing.assert_array_equal(icm.B, icm.task_covariance)
     np.testing.assert_array_equal(icm.effective_scales, [1.0, 2.0, 3.0])
     assert icm.W.shape == (3, 1) and icm.params.shape == (2,)
+
+
+def _trained_stub():
+    from mojogp_b200.gp import TrainingResult
+    gp = SingleOutputGP(RBF())
+    gp.dim = 2
+    gp._training_result = TrainingResult(params=np.ones(2, np.float32), noise=0.1, mean=0.0,
+                                         nll=1.0, iterations=1, converged=False,
+                                         nll_history=np.array([1.0]))
+    return gp
+
+
+def test_single_output_predict_argument_checks():
+    """Checks that precede any device work (gp.py:2500-2525)."""
+    gp = _trained_stub()
+    X = np.zeros((3, 2), np.float32)
+    with pytest.raises(ValueError, match="Only one of return_var or return_std"):
+        gp.predict(X, return_var=True, return_std=True)
+    with pytest.raises(ValueError, match="variance_method"):
+        gp.predict(X, variance_method="fast")
+    with pytest.raises(ValueError, match="target must be"):
+        gp.predict(X, target="both")
+    with pytest.raises(ValueError, match="exact_prediction_block_cols"):
+        gp.predict(X, exact_prediction_block_cols=0)
+    with pytest.raises(ValueError, match="features"):
+        gp.predict(np.zeros((3, 5), np.float32))
+    with pytest.raises(ValueError, match="X_test contains NaN"):
+        gp.predict(np.full((3, 2), np.nan, np.float32))
+    assert gp.is_trained and gp.nll_history.tolist() == [1.0]
+    assert gp.param_names == ["rbf_lengthscale", "rbf_outputscale"] and gp.num_params == 2
+    with pytest.raises(RuntimeError, match="scoring"):
+        SingleOutputGP(RBF()).score(X, np.zeros(3))
+
+
+def test_observation_noise_checks():
+    from mojogp_b200.gp import _checked_observation_noise
+    np.testing.assert_allclose(_checked_observation_noise([0.1, 0.2], 2), [0.1, 0.2], rtol=1e-7)
+    with pytest.raises(ValueError, match="requires observation_noise"):
+        _checked_observation_noise(None, 2)
+    with pytest.raises(ValueError, match=r"shape \(2,\)"):
+        _checked_observation_noise(np.ones(3), 2)
+    with pytest.raises(ValueError, match="NaN or Inf"):
+        _checked_observation_noise([np.inf, 0.1], 2)
+    with pytest.raises(ValueError, match="noise_floor"):
+        _checked_observation_noise([0.0, 0.1], 2)
