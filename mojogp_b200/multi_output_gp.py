@@ -60,6 +60,58 @@ def _named(kernel, params, pick) -> np.ndarray:
     return np.asarray([float(params[i]) for i, nm in enumerate(names) if pick(nm)], np.float32)
 
 
+def _observed_noise_matrix(m: int, T: int, observation_noise) -> np.ndarray:
+    """Explicit test-point noise [m, T] for observed multi-output prediction
+    (_resolve_observed_noise_matrix, multi_output_gp.py:553-601; grouped test
+    noise belongs to the grouped-noise models, which are not built)."""
+    if observation_noise is None:
+        raise ValueError("Observed multi-output prediction requires explicit observation_noise "
+                         "or noise_group_test; training noise is not reused for new points")
+    noise = np.ascontiguousarray(observation_noise, dtype=np.float32)
+    if noise.shape != (m, T):
+        raise ValueError(f"observation_noise must have shape ({m}, {T}), got {noise.shape}")
+    if not np.all(np.isfinite(noise)):
+        raise ValueError("observed prediction noise contains NaN or Inf values")
+    if np.any(noise <= 0):
+        raise ValueError("observed prediction noise values must be > 0")
+    return noise
+
+
+def _observed_output(latent: "MultiOutputPredictionResult", noise: np.ndarray,
+                     return_var: bool, return_std: bool):
+    """latent variance + test noise (_format_observed_prediction, multi_output_gp.py:604-625)."""
+    var = std = None
+    if latent.variance is not None:
+        var = np.ascontiguousarray(latent.variance + noise, dtype=np.float32)
+        std = np.sqrt(var)
+    if return_var:
+        return latent.mean, var
+    if return_std:
+        return latent.mean, std
+    return MultiOutputPredictionResult(mean=latent.mean, variance=var, std=std)
+
+
+class _ObservedPredictionMixin:
+    """predict_latent / predict_observed of the multi-output models
+    (multi_output_gp.py:2693-2740, 5558-5609)."""
+
+    def predict_latent(self, X_test, return_var: bool = False, return_std: bool = False,
+                       variance_method: str = "love", **kwargs):
+        return self.predict(X_test, return_var=return_var, return_std=return_std,
+                            variance_method=variance_method, **kwargs)
+
+    def predict_observed(self, X_test, observation_noise=None, noise_group_test=None,
+                         return_var: bool = False, return_std: bool = False,
+                         variance_method: str = "love", **kwargs):
+        if noise_group_test is not None:
+            raise NotImplementedError("noise_group_test needs a grouped-noise model, which is "
+                                      "not built; pass observation_noise [m, T]")
+        latent = self.predict(X_test, variance_method=variance_method, **kwargs)
+        noise = _observed_noise_matrix(latent.mean.shape[0], latent.mean.shape[1],
+                                       observation_noise)
+        return _observed_output(latent, noise, return_var, return_std)
+
+
 def _prediction_output(mean, var, return_var: bool, return_std: bool):
     """The multi-output predict return convention: (mean, std) with return_std,
     (mean, variance) with return_var (zeros when no variance was computed),
@@ -240,7 +292,7 @@ class LMC:
             pass
 
 
-class MultiOutputLMCGP:
+class MultiOutputLMCGP(_ObservedPredictionMixin):
     """LMC multi-output GP with heterogeneous latent kernels."""
 
     def __init__(self, kernels: list, num_probes: int = 10, max_cg_iterations: int = 200,
@@ -563,7 +615,7 @@ def _icm_initial_W(T: int, R: int, seed: int = 42) -> np.ndarray:
     return W.reshape(T, R)
 
 
-class MultiOutputGP:
+class MultiOutputGP(_ObservedPredictionMixin):
     """Multi-output GP with ICM task covariance, matrix-free on B200.
 
     Mirrors the reference's MultiOutputGP (mojogp/multi_output_gp.py:859-2520)

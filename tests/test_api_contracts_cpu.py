@@ -277,3 +277,24 @@ def test_observation_noise_checks():
         _checked_observation_noise([np.inf, 0.1], 2)
     with pytest.raises(ValueError, match="noise_floor"):
         _checked_observation_noise([0.0, 0.1], 2)
+
+
+def test_multi_output_observed_prediction_helpers():
+    from mojogp_b200.multi_output_gp import (MultiOutputPredictionResult, _observed_noise_matrix,
+                                             _observed_output)
+    noise = _observed_noise_matrix(2, 3, np.full((2, 3), 0.5))
+    lat = MultiOutputPredictionResult(mean=np.zeros((2, 3)), variance=np.full((2, 3), 1.5))
+    r = _observed_output(lat, noise, False, False)
+    np.testing.assert_allclose(r.variance, 2.0) and np.testing.assert_allclose(r.std, np.sqrt(2))
+    assert _observed_output(lat, noise, True, False)[1].shape == (2, 3)
+    with pytest.raises(ValueError, match="requires explicit observation_noise"):
+        _observed_noise_matrix(2, 3, None)
+    with pytest.raises(ValueError, match=r"shape \(2, 3\)"):
+        _observed_noise_matrix(2, 3, np.ones(2))
+    with pytest.raises(ValueError, match="> 0"):
+        _observed_noise_matrix(2, 3, np.zeros((2, 3)))
+    gp = MultiOutputLMCGP(kernels=["rbf"])
+    with pytest.raises(RuntimeError, match="trained"):
+        gp.predict_observed(np.zeros((2, 2)), np.ones((2, 3)))
+    with pytest.raises(NotImplementedError):
+        gp.predict_observed(np.zeros((2, 2)), noise_group_test=np.zeros(2))
