@@ -92,8 +92,32 @@ def _observed_output(latent: "MultiOutputPredictionResult", noise: np.ndarray,
 
 
 class _ObservedPredictionMixin:
-    """predict_latent / predict_observed of the multi-output models
-    (multi_output_gp.py:2693-2740, 5558-5609)."""
+    """Members the two multi-output models share: is_trained / training_result
+    (multi_output_gp.py:1396-1430, 4634-4671), score (2753-2788) and
+    predict_latent / predict_observed (2693-2740, 5558-5609)."""
+
+    @property
+    def is_trained(self) -> bool:
+        return getattr(self, "_lmc", None) is not None and \
+            getattr(self, "nll_history", None) is not None
+
+    @property
+    def training_result(self):
+        """The fitted model itself (its properties carry the result fields), or None."""
+        return self if self.is_trained else None
+
+    def score(self, X_test, Y_test) -> dict:
+        """rmse, mae, r2 over all tasks and rmse_per_task of the predictive mean."""
+        if not self.is_trained:
+            raise RuntimeError("GP must be trained before scoring. Call fit() first.")
+        Y = np.ascontiguousarray(Y_test, dtype=np.float32)
+        mean = self.predict(X_test, variance_method="mean_only").mean
+        res = Y - mean
+        ss_res = float(np.sum(res ** 2))
+        ss_tot = float(np.sum((Y - Y.mean(axis=0)) ** 2))
+        return {"rmse": float(np.sqrt(np.mean(res ** 2))), "mae": float(np.mean(np.abs(res))),
+                "r2": float(1.0 - ss_res / (ss_tot + 1e-10)),
+                "rmse_per_task": np.sqrt(np.mean(res ** 2, axis=0))}
 
     def predict_latent(self, X_test, return_var: bool = False, return_std: bool = False,
                        variance_method: str = "love", **kwargs):
@@ -499,6 +523,11 @@ class MultiOutputLMCGP(_ObservedPredictionMixin):
     @property
     def params_per_latent(self) -> list:
         return [np.asarray(p) for p in self.params_]
+
+    @property
+    def task_covariance(self) -> Optional[np.ndarray]:
+        """B = sum_s A_s [T, T], None before fit (multi_output_gp.py:4659-4663)."""
+        return self.B if getattr(self, "A", None) is not None else None
 
     @property
     def A_matrices(self) -> np.ndarray:

@@ -298,3 +298,13 @@ def test_multi_output_observed_prediction_helpers():
         gp.predict_observed(np.zeros((2, 2)), np.ones((2, 3)))
     with pytest.raises(NotImplementedError):
         gp.predict_observed(np.zeros((2, 2)), noise_group_test=np.zeros(2))
+
+
+def test_multi_output_trained_state_members():
+    gp = MultiOutputLMCGP(kernels=["rbf"])
+    assert gp.is_trained is False and gp.training_result is None
+    assert gp.task_covariance is None
+    with pytest.raises(RuntimeError, match="scoring"):
+        gp.score(np.zeros((2, 2)), np.zeros((2, 2)))
+    icm = MultiOutputGP(kernel="rbf")
+    assert icm.is_trained is False and icm.training_result is None
