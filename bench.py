@@ -49,16 +49,18 @@ def parse():
     ap.add_argument("--rhs", dest="t", type=int, default=16)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
-    ap.add_argument("--workload", default="c3", choices=["c1", "c2", "c3", "c4", "c5"],
-                    help="c3: the headline K·V / fit line (default); c1, c2, c4: the other "
+    ap.add_argument("--workload", default="c3", choices=["c1", "c2", "c3", "c3fit", "c4", "c5"],
+                    help="c3: the headline K·V / fit line (default); c3fit: the config-3 fit alone "
+                         "(--cfg-iters iterations, rows sharded); c1, c2, c4: the other "
                          "fit configurations (1 GPU); c5: LOVE prediction at scale")
     ap.add_argument("--cfg-iters", type=int, default=50,
                     help="c1 / c2 / c4: outer fit iterations")
     ap.add_argument("--test-rows", type=int, default=0,
                     help="c5: test points (default = --rows)")
     ap.add_argument("--love-rank", type=int, default=256)
-    ap.add_argument("--fit-iters", type=int, default=3,
-                    help="outer fit iterations timed for fit s/iter (0 = skip)")
+    ap.add_argument("--fit-iters", type=int, default=2,
+                    help="outer fit iterations for the fit block of the c3 line (0 = skip); "
+                         "--workload c3fit runs the full fit")
     return ap.parse_args()
 
 
@@ -105,6 +107,39 @@ class ClockSampler:
         return {"sm_mhz": statistics.median(sm) if sm else None,
                 "sm_max_mhz": max(smax) if smax else None,
                 "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def run_fit(X, y, iters: int, local: int, comm) -> dict:
+    """SingleOutputGP(RBF(ard=True)).fit(X, y, method="matrix_free",
+    num_probes=15) for `iters` outer iterations; s/iter is the median host wall
+    time per iteration over iterations 5..K (jit_training.mojo:855-860) when
+    K > 5, else over all K (labelled)."""
+    from mojogp_b200.gp import SingleOutputGP
+    from mojogp_b200.kernel import RBF
+    gp = SingleOutputGP(RBF(ard=True), device=local)
+    t0 = time.perf_counter()
+    res = gp.fit(X, y, max_iterations=iters, method="matrix_free", num_probes=15, comm=comm)
+    total = time.perf_counter() - t0
+    it = np.asarray(res.iter_times_ms, np.float64) / 1e3
+    window = "iterations 5..K" if it.size > 5 else f"all {it.size} iterations"
+    s_iter = float(np.median(it[4:] if it.size > 5 else it))
+    if comm:
+        s_iter = comm.allreduce_max(s_iter)
+        total = comm.allreduce_max(total)
+    info = gp._train_info
+    kinds = info.get("tile_kernels", [])
+    return {"s_per_iter": s_iter, "window": window, "iterations": int(res.iterations),
+            "fit_total_s": total,
+            "cg_iters_per_iter": [int(c) for c in res.cg_iterations_history],
+            "tile_kernel_per_iter": {k: kinds.count(k) for k in sorted(set(kinds))},
+            "settings": {"api": "SingleOutputGP(RBF(ard=True)).fit(method='matrix_free', "
+                                "num_probes=15)", "max_cg_iter": info["max_cg_iterations"],
+                         "cg_tol": info["cg_tolerance"],
+                         "max_tridiag_iter": info["max_tridiag_iter"],
+                         "precond_rank": info["precond_rank"], "initial_noise": 0.1},
+            "final_nll": float(res.nll),
+            "history": {"iter_s": it.tolist(), "nll": [float(v) for v in res.nll_history],
+                        "tile_kernels": kinds}}
 
 
 def run_reference(args, rank: int, world: int) -> None:
@@ -219,6 +254,35 @@ def run_love(args, rank: int, world: int, local: int) -> None:
         comm.close()
 
 
+def run_c3fit(args, rank: int, world: int, local: int) -> None:
+    """Config 3 fit alone: the public API at the reference's defaults for
+    --cfg-iters outer iterations, rows sharded over the ranks (north_star's
+    50-iteration fit at n = 1e6, d = 16)."""
+    from mojogp_b200 import synthetic
+    comm = None
+    if world > 1:
+        from mojogp_b200.distributed import Communicator
+        comm = Communicator.from_env(device=local)
+    X, y, _ = synthetic.config3(n=args.n, d=args.d)
+    sampler = ClockSampler(local)
+    sampler.start()
+    fit = run_fit(X, y, args.cfg_iters, local, comm)
+    clocks = sampler.stop()
+    line = {
+        "metric": "fit s/iter", "value": fit["s_per_iter"], "unit": "s", "n_gpus": world,
+        "steps": fit["iterations"], "warmup": 0, "ms_per_step": fit["s_per_iter"] * 1e3,
+        "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (config 3 recipe: X~N(0,I), y = RFF prior draw + noise, seed 3)",
+        "config": {"workload": "config3 fit RBF-ARD matrix-free, t=16", "n": args.n,
+                   "d": args.d, "parallelism": f"row-shard x{world}"},
+        "fit": fit, "clocks": clocks,
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if comm:
+        comm.close()
+
+
 def run_config(args, rank: int, world: int, local: int) -> None:
     """Configs 1, 2 and 4 through the public model API on one GPU: a full fit
     (fit s/iter = median per-iteration time; the LMC fit, which records no
@@ -319,6 +383,9 @@ def main():
     if args.workload in ("c1", "c2", "c4"):
         run_config(args, rank, world, local)
         return
+    if args.workload == "c3fit":
+        run_c3fit(args, rank, world, local)
+        return
 
     from mojogp_b200 import _lib, synthetic
     from mojogp_b200.kernel import RBF, make_ard_kernel
@@ -387,24 +454,15 @@ def main():
     else:
         e2e_tf = comm.e2e_sharded(prov, Vc, t, r0, r1, flops_total)
 
-    # Fit s/iter: full BBMM outer iterations (probes, mBCG with t = 16, SLQ,
-    # fused gradients, Adam) on the same inputs, rows sharded like the matvec.
+    # Fit s/iter through the public model API at the reference's resolved
+    # defaults for this route (gp.py:800-807, 1437-1456: max CG 100, tol 1e-2,
+    # max_tridiag 30, no preconditioner for matrix-free RBF-ARD; initial noise
+    # 0.1 and default kernel parameters), 15 probes (t = 16), rows sharded like
+    # the matvec.
     fit = None
     if args.fit_iters > 0:
-        from mojogp_b200 import engine
-        y = y_fit
-        res = engine.train(prov, y, max_iterations=args.fit_iters, learning_rate=0.01,
-                           num_probes=15, max_cg_iter=30, cg_tol=1e-2, precond_rank=0,
-                           use_preconditioner=False, max_tridiag_iter=30,
-                           init_mean=float(y.mean()), comm=comm)
-        it_s = float(np.median(res["iter_times_ms"])) / 1e3
-        if comm:
-            it_s = comm.allreduce_max(it_s)
-        fit = {"s_per_iter": it_s, "iters_timed": int(args.fit_iters),
-               "cg_iters_per_iter": [int(c) for c in res["cg_iterations_history"]],
-               "num_probes": 15, "precond_rank": 0,
-               "note": "median host wall time per outer iteration over the timed iterations (probes, mBCG capped at 30 "
-                       "iterations = max_tridiag, SLQ, fused gradients, Adam)"}
+        fit = run_fit(X, y_fit, args.fit_iters, local, comm)
+        fit.pop("history", None)
 
     achieved = flops_local / (kmean * 1e-3) / 1e12
     layout = prov.matvec_layout(t)

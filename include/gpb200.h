@@ -86,6 +86,10 @@ const char* gpb_version(void);
 /* Copies the calling thread's last error message into buf (NUL-terminated). */
 int gpb_last_error(char* buf, int64_t buf_len);
 int gpb_device_count(int32_t* count_out);
+/* Free and total device memory in bytes (cudaMemGetInfo) on `device`; no
+ * reference counterpart (memory planning for row shards and for callers that
+ * budget device memory up front). */
+int gpb_device_mem_info(int32_t device, int64_t* free_out, int64_t* total_out);
 
 /* Plain device-memory helpers so a NumPy host (no torch) can own device
  * buffers for the provider calls. */
@@ -236,6 +240,8 @@ typedef struct {
   int32_t precond_build_count;
   double precond_build_ms;
   int32_t precond_rank;
+  int32_t* tile_layouts; /* [max_iterations] tile kernel of the 16-column K.V chunks in each
+                            iteration (gpb_matvec_layout codes), or NULL */
 } gpb_train_result;
 
 int gpb_train(gpb_provider* p, gpb_comm* comm, const float* y_host, int64_t n,
@@ -249,6 +255,19 @@ int gpb_bbmm(gpb_provider* p, gpb_comm* comm, const float* y_centered_host, int6
              int32_t num_probes, int32_t max_cg_iter, int32_t max_tridiag_iter, float cg_tol,
              int32_t precond_rank, int32_t iteration, double* nll_out, double* grads_out,
              double* logdet_out, double* inv_quad_out, int32_t* cg_iters_out);
+
+/* The greedy pivoted-Cholesky pivots at the provider's current parameters:
+ * the preconditioner build of gpb_bbmm / gpb_train (precond_method 0,
+ * pivoted_cholesky.mojo:772-1050 with the argmax of 500-609: largest residual
+ * diagonal among unused rows, lowest index on ties, stop when it falls below
+ * 1e-10) run alone. pivots_out / values_out (values_out may be NULL) receive,
+ * in pick order, up to `rank` global row indices and the residual diagonal
+ * each was picked at; *actual_rank_out = how many were accepted. The
+ * reference keeps its pivots internal; this entry point exists so callers and
+ * tests can compare pivot lists. With comm != NULL the rows are sharded and
+ * every rank returns the same list. */
+int gpb_precond_pivots(gpb_provider* p, gpb_comm* comm, int32_t rank, int64_t* pivots_out,
+                       float* values_out, int32_t* actual_rank_out);
 
 /* Host-only numerics exposed for testing (no GPU needed): the SLQ
  * log-determinant from per-probe tridiagonals (diags [num_probes][m],
@@ -373,18 +392,23 @@ int gpb_tc_selftest(int32_t device, int32_t variant, const float* a_host, const 
  * (tensor-core distances, fp32 CUDA-core contraction; 1-column chunks). */
 int gpb_matvec_layout(gpb_provider* p, int64_t ncols, int32_t* layout);
 
-/* Same result as gpb_forward_matvec, but the call allocates no device memory:
- * all scratch lives in one fixed 32 MiB array compiled into the library, held
- * on every GPU that uses it until the process exits. For callers that must
- * not allocate while they run (an external memory pool or arena, or code where
- * an allocation's implicit synchronisation is not allowed). No counterpart in
- * the reference. Limit: n * DP + round_up(n, 128) * W floats must fit in
- * 8 Mi floats (DP = padded input dims, W = packed row width, 2 * (DP + 16)
- * for 16 right-hand sides: about 100k rows at d = 16); larger n is
- * rejected with GPB_ERR_INVALID. The first call on a device looks up the
- * array's device address, so make that first call before any stream capture.
- * Calls share the array: calls that overlap on the GPU race and must be
- * ordered by the caller. */
+/* Same result as gpb_forward_matvec, on the same tile kernel, but the call
+ * allocates no device memory: all scratch lives in one fixed 32 MiB array
+ * compiled into the library, held on every GPU that uses it until the process
+ * exits. For callers that must not allocate while they run (an external
+ * memory pool or arena, or code where an allocation's implicit
+ * synchronisation is not allowed). No counterpart in the reference.
+ * Limit: 64 + S + round_up(n, 128) * W floats must fit in 8 Mi floats, where
+ * W is the widest packed row over the call's 16-column chunks (72 on the Gram
+ * layout at d <= 16, t = 16; 80 at d 17..32 when a 5..8-column chunk follows)
+ * and S = n * DP (DP = padded input dims) only when the provider's prescaled
+ * inputs are stale (no product since the last parameter update). That is
+ * about 116k rows at d = 16, t = 16 (95k when stale) and 104k rows at d = 32
+ * (75k when stale); larger n is rejected with GPB_ERR_INVALID. A stale call
+ * reduces the input norms itself, with one stream synchronisation. The first
+ * call on a device loads the array's module, so make that first call before
+ * any stream capture. Calls share the array: calls that overlap on the GPU
+ * race and must be ordered by the caller. */
 int gpb_forward_matvec_noalloc(gpb_provider* p, float* out_dev, const float* v_dev, int64_t ncols);
 
 #ifdef __cplusplus

@@ -64,6 +64,7 @@ SIGNATURES = {
     "gpb_benchmark_forward_sharded": [P, P, P, c_i64, c_i32, c_i32, c_i32, P, P, P],
     "gpb_train": [P, P, P, c_i64, P, P],
     "gpb_bbmm": [P, P, P, c_i64, c_i32, c_i32, c_i32, c_f32, c_i32, c_i32, P, P, P, P, P],
+    "gpb_precond_pivots": [P, P, c_i32, P, P, PI32],
     "gpb_slq_logdet": [P, P, c_i32, c_i32, c_i64, P],
     "gpb_tridiag_eig": [P, P, c_i32, P, P],
     "gpb_hash_gaussian": [c_i32, P, c_i64, C.c_uint64],
@@ -73,6 +74,7 @@ SIGNATURES = {
     "gpb_predict_with_cache": [P, P, c_i64, P, P],
     "gpb_prediction_cache_destroy": [P],
     "gpb_forward_matvec_noalloc": [P, P, P, c_i64],
+    "gpb_device_mem_info": [c_i32, P, P],
     "gpb_tc_selftest": [c_i32, c_i32, P, P, P],
     "gpb_predict_exact_variance": [P, P, P, c_i64, c_i32, c_i32, c_f32, c_i32, P, PI32],
     "gpb_lmc_create": [P, c_i32, c_i32, PP],

@@ -88,7 +88,7 @@ __global__ void __launch_bounds__(256) pc_argmax_kernel(const float* __restrict_
 // pivot's row of L (this rank's contribution; all-reduced when sharded).
 __global__ void pc_pivot_kernel(const unsigned long long* result, int m, int64_t r0, int64_t nl,
                                 int* done, int* actual_rank, float* mask, const float* L,
-                                float* lrow, float* pivinfo) {
+                                float* lrow, float* pivinfo, int64_t* piv_out, float* val_out) {
   const unsigned long long key = *result;
   const bool was_done = *done != 0;
   const float maxv = key ? from_ordered_bits((uint32_t)(key >> 32)) : -1e30f;
@@ -109,6 +109,8 @@ __global__ void pc_pivot_kernel(const unsigned long long* result, int m, int64_t
     if (owner) mask[piv - r0] = 0.f;
     pivinfo[0] = (float)piv;  // exact for n < 2^24, as in the reference
     pivinfo[1] = maxv;
+    piv_out[m] = piv;
+    val_out[m] = maxv;
     *actual_rank = m + 1;
   }
 }
@@ -152,6 +154,10 @@ int precond_build(Engine& E, int rank_req, Precond& P, bool finalize) {
   GPB_TRY(P.mask.ensure((size_t)std::max<int64_t>(nl, 1) * sizeof(float)));
   GPB_TRY(P.scratch.ensure(4096 + (size_t)rmax * sizeof(float)));
   GPB_TRY(P.keys.ensure(sizeof(unsigned long long) * 512));
+  GPB_TRY(P.piv.ensure((size_t)rmax * (sizeof(int64_t) + sizeof(float))));
+  int64_t* piv_out = (int64_t*)P.piv.ptr;
+  float* val_out = (float*)(piv_out + rmax);
+  GPB_CHECK_CUDA(cudaMemsetAsync(P.piv.ptr, 0, P.piv.bytes, E.st));
   cudaStream_t st = E.st;
   char* base = (char*)P.scratch.ptr;
   unsigned long long* result = (unsigned long long*)base;        // 8 B
@@ -178,7 +184,7 @@ int precond_build(Engine& E, int rank_req, Precond& P, bool finalize) {
       GPB_REQUIRE(r == ncclSuccess, GPB_ERR_NCCL, "argmax all-reduce: %s", ncclGetErrorString(r));
     }
     pc_pivot_kernel<<<1, 256, 0, st>>>(result, m, E.r0, nl, done, actual, P.mask.f(), P.L.f(),
-                                       lrow, pivinfo);
+                                       lrow, pivinfo, piv_out, val_out);
     GPB_CHECK_CUDA(cudaGetLastError());
     if (E.dist.world > 1 && m > 0) GPB_TRY(E.allreduce_sum_f(lrow, (size_t)m));
     pc_column_kernel<<<nb, bs, 0, st>>>(p->X_d, p->d, E.r0, nl, p->dk, done, result, lrow, m,

@@ -15,6 +15,8 @@ struct Precond {
   DBuf Minv;            // [rank][rank] float
   DBuf u;               // [t][rank] work
   DBuf diag, mask, scratch, keys;
+  DBuf piv;             // [rank] int64 pivot indices in pick order, then [rank] float
+                        // residual diagonal at each pick
   LmcPrecond* lmc = nullptr;  // when set, apply / sample / logdet are the LMC ones
 };
 

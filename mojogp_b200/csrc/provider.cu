@@ -210,6 +210,13 @@ __global__ void max_sqnorm_kernel(const float* __restrict__ xs, int64_t n, int D
   if ((threadIdx.x & 31) == 0) atomicMax(out, s != s ? 0xFFFFFFFFu : __float_as_uint(s));
 }
 
+int launch_max_sqnorm(const float* xs, int64_t n, int DP, unsigned* word, cudaStream_t st) {
+  if (n <= 0) return GPB_OK;
+  max_sqnorm_kernel<<<(unsigned)ceil_div(n, 256), 256, 0, st>>>(xs, n, DP, word);
+  GPB_CHECK_CUDA(cudaGetLastError());
+  return GPB_OK;
+}
+
 int provider_refresh_xs(gpb_provider* p) {
   if (!p->xs_dirty) return GPB_OK;
   if (p->Xs_d) cudaFree(p->Xs_d);
@@ -381,6 +388,16 @@ int gpb_device_count(int32_t* count_out) {
     c = 0;
   }
   *count_out = c;
+  return GPB_OK;
+}
+
+int gpb_device_mem_info(int32_t device, int64_t* free_out, int64_t* total_out) {
+  GPB_REQUIRE(free_out && total_out, GPB_ERR_INVALID, "null output");
+  GPB_CHECK_CUDA(cudaSetDevice(device));
+  size_t f = 0, t = 0;
+  GPB_CHECK_CUDA(cudaMemGetInfo(&f, &t));
+  *free_out = (int64_t)f;
+  *total_out = (int64_t)t;
   return GPB_OK;
 }
 

@@ -65,6 +65,9 @@ namespace gpb {
 int provider_plan(gpb_provider* p);
 // Ensure Xs_d matches the current params.
 int provider_refresh_xs(gpb_provider* p);
+// atomicMax of the bit patterns of |xs_i|^2 over n prescaled rows into *word
+// (which the caller zeroes first; NaN maps to 0xFFFFFFFF).
+int launch_max_sqnorm(const float* xs, int64_t n, int DP, unsigned* word, cudaStream_t st);
 // Check and clear the device error word (synchronizes the stream).
 int provider_check_device_error(gpb_provider* p);
 // out[c][i] = k(x_{r0 + i}, x*_c) for i < nl, c < m (raw inputs; xt_dev [m][d] on the device).

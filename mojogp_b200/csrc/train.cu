@@ -407,6 +407,7 @@ int train_loop(Engine& E, const float* y_host_local, const gpb_train_options& o,
                       o.cg_tol, it, it > 0, R));
     const float nll = (float)R.nll;
     if (res.cg_iterations) res.cg_iterations[it] = R.cg_iters;
+    if (res.tile_layouts) res.tile_layouts[it] = kv_layout(p->eval, p->DP, 16, p->gram_ok);
     if (nll != nll) {
       lr *= 0.5f;
       if (o.verbose) std::printf("  NaN NLL at iteration %d - halving LR to %g\n", it, lr);
@@ -647,6 +648,37 @@ int gpb_bbmm(gpb_provider* p, gpb_comm* comm, const float* y_centered_host, int6
   if (logdet_out) *logdet_out = R.logdet;
   if (inv_quad_out) *inv_quad_out = R.inv_quad;
   if (cg_iters_out) *cg_iters_out = R.cg_iters;
+  return provider_check_device_error(p);
+}
+
+int gpb_precond_pivots(gpb_provider* p, gpb_comm* comm, int32_t rank, int64_t* pivots_out,
+                       float* values_out, int32_t* actual_rank_out) {
+  clear_error();
+  GPB_REQUIRE(p && pivots_out && actual_rank_out && rank >= 1, GPB_ERR_INVALID, "bad arguments");
+  GPB_CHECK_CUDA(cudaSetDevice(p->device));
+  Engine E;
+  GPB_TRY(engine_from_comm(p, comm, E));
+  Precond P;
+  GPB_TRY(precond_build(E, rank, P, false));
+  const int rmax = (int)std::min<int64_t>(rank, E.n);
+  const int got = std::min(P.rank, rmax);
+  std::vector<int64_t> piv(rmax);
+  std::vector<float> val(rmax);
+  GPB_CHECK_CUDA(cudaMemcpyAsync(piv.data(), P.piv.ptr, rmax * sizeof(int64_t),
+                                 cudaMemcpyDeviceToHost, E.st));
+  GPB_CHECK_CUDA(cudaMemcpyAsync(val.data(), (const int64_t*)P.piv.ptr + rmax,
+                                 rmax * sizeof(float), cudaMemcpyDeviceToHost, E.st));
+  GPB_CHECK_CUDA(cudaStreamSynchronize(E.st));
+  // The termination rule may report rank 1 with no accepted pivot (a zero
+  // kernel); only picks the kernel accepted are returned.
+  int accepted = 0;
+  for (int m = 0; m < got; ++m) {
+    if (!(val[m] >= 1e-10f)) break;
+    pivots_out[m] = piv[m];
+    if (values_out) values_out[m] = val[m];
+    ++accepted;
+  }
+  *actual_rank_out = accepted;
   return provider_check_device_error(p);
 }
 

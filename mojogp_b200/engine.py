@@ -54,6 +54,7 @@ class TrainResult(C.Structure):
         ("precond_build_count", C.c_int32),
         ("precond_build_ms", C.c_double),
         ("precond_rank", C.c_int32),
+        ("tile_layouts", C.c_void_p),
     ]
 
 
@@ -93,6 +94,8 @@ def train(provider: Provider, y: np.ndarray, *, max_iterations: int = 100,
     res.iter_times_ms = _p(times).value
     res.cg_iterations = _p(cg_it).value
     res.alpha = _p(alpha).value
+    layouts = np.full(max(max_iterations, 1), -1, np.int32)
+    res.tile_layouts = _p(layouts).value
     _lib.call("gpb_train", provider.h, C.c_void_p(comm.handle) if comm else None, _p(y),
               provider.n, C.byref(opt), C.byref(res))
     it = int(res.iterations)
@@ -112,6 +115,7 @@ def train(provider: Provider, y: np.ndarray, *, max_iterations: int = 100,
         "precond_build_count": int(res.precond_build_count),
         "precond_build_time_ms": float(res.precond_build_ms),
         "precond_rank": int(res.precond_rank),
+        "tile_kernels": [Provider.LAYOUTS.get(int(v), str(int(v))) for v in layouts[:it]],
     }
 
 
@@ -187,6 +191,18 @@ def bbmm(provider: Provider, y_centered: np.ndarray, *, num_probes: int = 10,
               iteration, C.byref(nll), _p(grads), C.byref(ld), C.byref(iq), C.byref(it))
     return {"nll": nll.value, "grads": grads, "logdet": ld.value, "inv_quad": iq.value,
             "cg_iters": it.value}
+
+
+def precond_pivots(provider: Provider, rank: int, comm=None) -> dict:
+    """Greedy pivoted-Cholesky pivots at the provider's parameters, in pick
+    order, with the residual diagonal each was picked at (the build that
+    gpb_bbmm / gpb_train run; pivoted_cholesky.mojo:500-609, 772-1050)."""
+    piv = np.zeros(max(int(rank), 1), np.int64)
+    val = np.zeros(max(int(rank), 1), np.float32)
+    got = C.c_int32()
+    _lib.call("gpb_precond_pivots", provider.h, C.c_void_p(comm.handle) if comm else None,
+              int(rank), _p(piv), _p(val), C.byref(got))
+    return {"pivots": piv[:got.value].copy(), "values": val[:got.value].copy()}
 
 
 PREDICT_MEAN_ONLY, PREDICT_LOVE, PREDICT_EXACT = 0, 1, 2

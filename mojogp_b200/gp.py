@@ -27,6 +27,21 @@ from . import engine, prediction
 from .kernel import KernelNode, KernelType, make_ard_kernel
 from .provider import Provider
 
+# Saved-artifact schema of the reference (gp.py:76).
+MODEL_SCHEMA_VERSION = 1
+
+
+def _package_version() -> str:
+    from . import __version__
+    return __version__
+
+
+def _artifact_base(path) -> str:
+    path = str(path)
+    if path.endswith(".json") or path.endswith(".npz"):
+        path = path.rsplit(".", 1)[0]
+    return path
+
 _DEFAULT_PREDICT_LANCZOS_RANK = 100
 _DEFAULT_ARD_PREDICT_LANCZOS_RANK = 200
 _DEFAULT_PREDICT_MAX_CG_ITER = 300
@@ -345,7 +360,8 @@ class SingleOutputGP:
                             "max_tridiag_iter": cg["max_tridiag_iter"],
                             "precond_rank": res["precond_rank"],
                             "precond_build_count": res["precond_build_count"],
-                            "precond_build_time_ms": res["precond_build_time_ms"]}
+                            "precond_build_time_ms": res["precond_build_time_ms"],
+                            "tile_kernels": res["tile_kernels"]}
         self._training_result = TrainingResult(
             params=res["params"], noise=res["noise"], mean=res["mean"], nll=res["final_nll"],
             iterations=res["iterations"], converged=res["converged"],
@@ -525,46 +541,124 @@ class SingleOutputGP:
         return float(self._training_result.mean)
 
     # -------------------------------------------------------------- persist
-    def save(self, path: str) -> None:
-        """JSON config + .npz arrays (training data, params, LOVE root)."""
-        if not self._is_trained:
-            raise RuntimeError("GP must be trained first.")
-        p = Path(path)
+    def _artifact_config(self) -> dict:
+        """The reference's `{path}_config.json` content (gp.py:3661-3707) for
+        this continuous-kernel model; keys the reference's load() reads
+        (gp.py:3735-3876) carry the same meaning here."""
         tr = self._training_result
-        cfg = {"format": "mojogp_b200/1", "kernel": self.kernel_spec.to_dict(), "ard": self.ard,
-               "dim": self.dim, "noise": float(tr.noise), "mean": float(tr.mean),
-               "nll": float(tr.nll), "iterations": int(tr.iterations),
-               "converged": bool(tr.converged), "lanczos_rank": int(tr.lanczos_rank),
-               "train_info": self._train_info}
-        arrays = {"X": self._X_train, "y": self._y_train, "params": tr.params}
+        return {
+            "schema_version": MODEL_SCHEMA_VERSION,
+            "mojogp_version": f"mojogp_b200 {_package_version()}",
+            "wrapper": "SingleOutputGP",
+            "dim": int(self.dim),
+            "ard": bool(self.ard),
+            "verbose": bool(self.verbose),
+            "cat_dims": {},
+            "cat_kernel": "ehh",
+            "kernel_tree": self.kernel_spec.to_dict(),
+            "is_mixed": False,
+            "training_method": self._training_method,
+            "engine_mean": None,
+            "backend_train_info": self._train_info or None,
+            "cached_love_method": None,
+            "noise_mode": "scalar" if self._obs_noise is None else "fixed_vector",
+            "noise_floor": 1e-6,
+            "noise_regularization": 0.0,
+            "noise_function": None,
+            "provider_noise_mode_int": None if self._obs_noise is None else 1,
+            "has_observation_noise_train": self._obs_noise is not None,
+            "has_observation_noise_fn": False,
+            "has_noise_group_train": False,
+            "has_group_noise": False,
+            "result_type": "TrainingResult",
+            "noise": float(tr.noise),
+            "mean": float(tr.mean),
+            "nll": float(tr.nll),
+            "iterations": int(tr.iterations),
+            "converged": bool(tr.converged),
+            "lanczos_rank": int(tr.lanczos_rank),
+        }
+
+    def save(self, path: str) -> None:
+        """Save the trained model in the reference's artifact layout
+        (gp.py:3648-3723): `{path}_config.json` and `{path}_arrays.npz` with
+        X_train, y_train, params (and observation_noise_train). A cached LOVE
+        root is stored as the extra array `lanczos_root`, which the
+        reference's load ignores. A trailing .json / .npz on `path` is
+        dropped, as in the reference."""
+        if not self._is_trained:
+            raise RuntimeError("GP must be trained before saving.")
+        base = _artifact_base(path)
+        tr = self._training_result
+        with open(f"{base}_config.json", "w") as f:
+            json.dump(self._artifact_config(), f, indent=2)
+        arrays = {"X_train": self._X_train, "y_train": self._y_train,
+                  "params": np.asarray(tr.params, np.float32)}
+        if self._obs_noise is not None:
+            arrays["observation_noise_train"] = self._obs_noise
         if tr.lanczos_root is not None:
             arrays["lanczos_root"] = tr.lanczos_root
-        if tr.nll_history is not None:
-            arrays["nll_history"] = tr.nll_history
-        if self._obs_noise is not None:
-            arrays["observation_noise"] = self._obs_noise
-        p.with_suffix(".json").write_text(json.dumps(cfg, indent=1))
-        np.savez_compressed(p.with_suffix(".npz"), **arrays)
+        np.savez(f"{base}_arrays.npz", **arrays)
+
+    @staticmethod
+    def read_artifact(path: str):
+        """Read and check a saved SingleOutputGP artifact (the reference's
+        checks and messages, gp.py:3735-3770); returns (config, arrays).
+        Needs no GPU."""
+        base = _artifact_base(path)
+        with open(f"{base}_config.json", "r") as f:
+            config = json.load(f)
+        wrapper = config.get("wrapper")
+        if wrapper != "SingleOutputGP":
+            raise ValueError(
+                "Saved model is not a SingleOutputGP artifact. "
+                f"Expected wrapper='SingleOutputGP', got {wrapper!r}.")
+        schema_version = int(config.get("schema_version", 0))
+        if schema_version != MODEL_SCHEMA_VERSION:
+            raise ValueError(
+                f"Unsupported SingleOutputGP schema_version={schema_version}; "
+                f"expected {MODEL_SCHEMA_VERSION}.")
+        if "kernel_tree" not in config:
+            raise ValueError("SingleOutputGP artifact is missing required kernel_tree.")
+        if config.get("is_mixed") or config.get("cat_dims"):
+            raise NotImplementedError("mixed / categorical kernels are not built")
+        if config.get("result_type", "TrainingResult") != "TrainingResult":
+            raise NotImplementedError(f"result_type {config.get('result_type')!r} is not built")
+        with np.load(f"{base}_arrays.npz", allow_pickle=False) as npz:
+            arrays = {k: npz[k] for k in npz.files}
+        return config, arrays
 
     @classmethod
-    def load(cls, path: str, device: int = 0) -> "SingleOutputGP":
-        p = Path(path)
-        cfg = json.loads(p.with_suffix(".json").read_text())
-        arr = np.load(p.with_suffix(".npz"))
-        gp = cls(KernelNode.from_dict(cfg["kernel"]), device=device)
-        gp.dim = cfg["dim"]
+    def load(cls, path: str, kernel: Optional[KernelNode] = None,
+             device: int = 0) -> "SingleOutputGP":
+        """Load an artifact written by save() here or by the reference's
+        SingleOutputGP.save (gp.py:3725-3910): the kernel comes from
+        `kernel_tree` unless given, the trained state from the config and
+        arrays; the provider is created on `device`."""
+        config, arrays = cls.read_artifact(path)
+        if kernel is None:
+            kernel = KernelNode.from_dict(config["kernel_tree"])
+        gp = cls(kernel, init_mean=config.get("init_mean"), verbose=config.get("verbose", False),
+                 device=device)
+        X = np.ascontiguousarray(arrays["X_train"], dtype=np.float32)
+        y = np.ascontiguousarray(arrays["y_train"], dtype=np.float32)
+        gp.dim = X.shape[1]
         gp.kernel = gp._resolved_kernel(gp.dim)
-        gp._X_train, gp._y_train = arr["X"], arr["y"]
-        gp._obs_noise = arr["observation_noise"] if "observation_noise" in arr else None
-        gp._train_info = cfg.get("train_info", {})
+        gp._X_train, gp._y_train = X, y
+        gp._obs_noise = (np.ascontiguousarray(arrays["observation_noise_train"], np.float32)
+                         if "observation_noise_train" in arrays else None)
+        gp._training_method = config.get("training_method")
+        gp._train_info = dict(config.get("backend_train_info") or {})
+        params = np.ascontiguousarray(arrays["params"], dtype=np.float32)
+        if params.shape[0] != gp.kernel.num_params():
+            raise ValueError(f"saved params have {params.shape[0]} entries, the kernel needs "
+                             f"{gp.kernel.num_params()}")
         gp._training_result = TrainingResult(
-            params=arr["params"], noise=cfg["noise"], mean=cfg["mean"], nll=cfg["nll"],
-            iterations=cfg["iterations"], converged=cfg["converged"],
-            lanczos_root=arr["lanczos_root"] if "lanczos_root" in arr else None,
-            lanczos_rank=cfg["lanczos_rank"],
-            nll_history=arr["nll_history"] if "nll_history" in arr else None)
-        gp._provider = Provider(gp._X_train, gp.kernel, arr["params"], cfg["noise"],
-                                device=device, noise_vector=gp._obs_noise)
+            params=params, noise=config["noise"], mean=config.get("mean", 0.0),
+            nll=config["nll"], iterations=config["iterations"], converged=config["converged"],
+            lanczos_root=arrays.get("lanczos_root"), lanczos_rank=config["lanczos_rank"])
+        gp._provider = Provider(X, gp.kernel, params, float(config["noise"]), device=device,
+                                noise_vector=gp._obs_noise)
         return gp
 
     def _destroy(self) -> None:
@@ -582,13 +676,6 @@ class SingleOutputGP:
             self._destroy()
         except Exception:
             pass
-
-
-def fit_gp(X, y, kernel: KernelNode, **kw) -> SingleOutputGP:
-    """Convenience: construct and fit a SingleOutputGP."""
-    gp = SingleOutputGP(kernel)
-    gp.fit(X, y, **kw)
-    return gp
 
 
 def fit_gp(X: np.ndarray, y: np.ndarray, kernel: Optional[KernelNode] = None,

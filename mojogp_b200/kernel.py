@@ -263,7 +263,8 @@ class KernelNode:
         d: dict = {}
         if self.is_leaf():
             d["kernel_type"] = self.kernel_type.name
-            d["ard"] = bool(self.ard)
+            if self.ard:
+                d["ard"] = True
             if self.ard_dim is not None:
                 d["ard_dim"] = int(self.ard_dim)
             if self.initial_values:

@@ -98,6 +98,45 @@ class Precond:
         return self.L @ zr + math.sqrt(self.noise) * zn
 
 
+def greedy_pivots(column, diag0: np.ndarray, rank: int, follow=None, dtype=np.float32) -> dict:
+    """The greedy pivot sequence of pivoted_cholesky.mojo:500-609 (argmax of
+    the residual diagonal over unused rows, lowest index on ties,
+    :537-539 / 573-577) and 772-1050 (stop below 1e-10; L[:, m] =
+    (K[:, piv] - L[:, :m] L[piv, :m]^T) / sqrt(d_piv); d -= L[:, m]^2 on
+    unused rows), with K given column by column: column(i) -> K[:, i].
+
+    With `follow` (a pivot list, e.g. the GPU's), step m records its own
+    argmax and then continues with follow[m], so every later step is checked
+    against the same residual diagonal the follower saw. Per step it returns
+    the own argmax `pivots`, its value, the followed pivot's value and `gap` =
+    (own value - followed value) / own value (0 when they agree)."""
+    n = diag0.shape[0]
+    diag = np.asarray(diag0, dtype).copy()
+    mask = np.ones(n, dtype=bool)
+    L = np.zeros((n, rank), dtype)
+    own, own_val, fol_val, gap = [], [], [], []
+    steps = rank if follow is None else min(rank, len(follow))
+    for m in range(steps):
+        cand = np.where(mask, diag, -np.inf)
+        piv = int(np.argmax(cand))
+        maxv = float(cand[piv])
+        if not (maxv >= 1e-10):
+            break
+        own.append(piv)
+        own_val.append(maxv)
+        use = piv if follow is None else int(follow[m])
+        uv = float(cand[use])
+        fol_val.append(uv)
+        gap.append(0.0 if use == piv else (maxv - uv) / maxv)
+        mask[use] = False
+        col = np.asarray(column(use), dtype) - L[:, :m] @ L[use, :m]
+        col = col / dtype(math.sqrt(max(uv, 1e-10)))
+        L[:, m] = col
+        diag[mask] -= col[mask] ** 2
+    return {"pivots": own, "values": np.asarray(own_val), "followed_values": np.asarray(fol_val),
+            "gap": np.asarray(gap)}
+
+
 def mbcg(A: np.ndarray, rhs: np.ndarray, max_iter: int, max_tridiag: int, tol: float,
          precond: Precond | None = None, x0: np.ndarray | None = None):
     """Batched preconditioned CG with tridiagonal capture (float64)."""

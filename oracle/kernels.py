@@ -58,14 +58,25 @@ def parse(spec):
 def _leaf(kt, ard, p, X1, X2, want_grad):
     """Returns K [n1, n2] and (if want_grad) list of dK/dtheta for leaf params."""
     nd = X1.shape[1]
-    diff = X1[:, None, :] - X2[None, :, :]  # [n1, n2, nd]
     grads = []
     if kt in (RBF, M12, M32, M52, RQ):
         nl = nd if ard else 1
         ell = p[:nd] if ard else np.full(nd, p[0])
-        dl = diff / ell
-        sq = dl * dl
-        s = sq.sum(axis=2)
+        if want_grad:
+            diff = X1[:, None, :] - X2[None, :, :]  # [n1, n2, nd]
+            dl = diff / ell
+            sq = dl * dl
+            s = sq.sum(axis=2)
+        else:
+            # Same sum, one input dim at a time: [n1, n2] memory instead of
+            # [n1, n2, nd], so row samples against 1e6 columns fit.
+            a1, a2 = X1 / ell, np.ascontiguousarray((X2 / ell).T)
+            s = np.zeros((X1.shape[0], X2.shape[0]))
+            dk = np.empty_like(s)
+            for k in range(nd):
+                np.subtract(a1[:, k, None], a2[k][None, :], out=dk)
+                np.multiply(dk, dk, out=dk)
+                s += dk
         if kt == RQ:
             alpha, os = p[nl], p[nl + 1]
             z = s / (2.0 * alpha)
@@ -110,6 +121,7 @@ def _leaf(kt, ard, p, X1, X2, want_grad):
             grads = g
         return K, grads
     if kt == PER:
+        diff = X1[:, None, :] - X2[None, :, :]  # [n1, n2, nd]
         nl = nd if ard else 1
         period, os = p[nl], p[nl + 1]
         ell = p[:nd] if ard else np.full(nd, p[0])

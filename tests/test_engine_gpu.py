@@ -121,3 +121,57 @@ def test_train_with_preconditioner_runs(gpb_lib):
     h = res["nll_history"]
     assert np.all(np.isfinite(h)) and h[-1] < h[0]
     assert res["precond_rank"] == 50 and res["precond_build_count"] >= 1
+
+
+def _pivot_check(prov, k, p, X, rank, tag):
+    """GPU pivot list vs the oracle's greedy rule (float32 factor, as the
+    reference's pivoted_cholesky.mojo). Pivots must be identical except at
+    near-ties: steps where the oracle's own pick and the GPU's differ by less
+    than 1e-6 of the residual diagonal. Those are listed in the failure text."""
+    from oracle import kernels as ok
+    got = engine.precond_pivots(prov, rank)
+    spec = k.to_spec(X.shape[1])
+    diag = np.array([ok.kernel_matrix(spec, p, X[i:i + 1])[0, 0] for i in range(1)])
+    diag = np.full(X.shape[0], diag[0])  # stationary kernel: constant diagonal
+    ref = ob.greedy_pivots(lambda i: ok.kernel_matrix(spec, p, X, X[i:i + 1])[:, 0], diag, rank,
+                           follow=got["pivots"])
+    gp = np.asarray(got["pivots"])
+    assert len(gp) == len(ref["pivots"]) == rank, (tag, len(gp), len(ref["pivots"]))
+    diff = np.nonzero(gp != np.asarray(ref["pivots"]))[0]
+    ties = [(int(m), int(gp[m]), int(ref["pivots"][m]), float(ref["gap"][m])) for m in diff]
+    assert all(g < 1e-6 for *_, g in ties), f"{tag}: pivots differ beyond near-ties: {ties}"
+    np.testing.assert_allclose(got["values"], ref["followed_values"], rtol=1e-3, atol=1e-5)
+    return ties
+
+
+def test_pivot_indices_match_oracle_small(gpb_lib):
+    X, y, k, p = _problem("rbf_ard", n=300)
+    prov = Provider(X, k, p, 0.02)
+    ties = _pivot_check(prov, k, p, X, 30, "rbf_ard n=300")
+    assert not ties
+
+
+def test_pivot_indices_match_oracle_config2_recipe(gpb_lib):
+    # Config-2 recipe (Matern-5/2 ARD, d = 8, X ~ U[0,1]^8, rank 100) at n = 2e4.
+    from mojogp_b200 import synthetic
+    X, y = synthetic.config2(n=20_000)
+    d = X.shape[1]
+    k = make_ard_kernel(Matern52(ard=True), d)
+    p = np.array([0.6, 0.8, 1.0, 0.7, 0.9, 1.1, 0.5, 0.75, 1.3], np.float32)
+    prov = Provider(X, k, p, 0.01)
+    ties = _pivot_check(prov, k, p, X, 100, "config2 n=2e4")
+    assert len(ties) <= 2, ties
+
+
+def test_pivot_index_exact_above_2_24(gpb_lib):
+    # Indices beyond 2^24 are not exactly representable in float32; the GPU
+    # keeps pivot indices as integers. X is a constant row except for one
+    # row near the end whose kernel-row residual stays largest after step 0.
+    n, d = (1 << 24) + 1000, 1
+    X = np.zeros((n, d), np.float32)
+    X[-3, 0] = 40.0    # far from every other row: picked second
+    k = RBF()
+    p = np.array([1.0, 1.0], np.float32)
+    prov = Provider(X, k, p, 0.01)
+    got = engine.precond_pivots(prov, 2)
+    assert list(got["pivots"]) == [0, n - 3]

@@ -86,3 +86,29 @@ def test_materialized_route_name_is_served(gpb_lib):
     b = SingleOutputGP(RBF()).fit(X, y, max_iterations=5, method="matrix_free",
                                   preconditioner_rank=100)
     np.testing.assert_allclose(a.nll_history, b.nll_history, rtol=0, atol=0)
+
+
+def test_load_reference_artifact_and_predict(gpb_lib, tmp_path):
+    """An artifact written by the reference's own SingleOutputGP.save
+    (tests/golden/make_saved_model.py) loads here and predicts the exact
+    posterior of its saved state (mean 1e-4; LOVE and exact variance 1e-4);
+    saving it again and loading that reproduces the predictions."""
+    from pathlib import Path
+    base = Path(__file__).resolve().parent / "golden" / "ref_rbf_ard"
+    gp = SingleOutputGP.load(str(base))
+    assert gp.dim == 3 and gp.ard
+    X, y = gp._X_train.astype(np.float64), gp._y_train.astype(np.float64)
+    Xs = np.random.default_rng(5).uniform(-1.2, 1.2, size=(40, 3)).astype(np.float32)
+    mu, var = _exact(gp, X, y, Xs.astype(np.float64))
+    mean, std = gp.predict(Xs, return_std=True, variance_method="exact")
+    np.testing.assert_allclose(mean, mu, rtol=1e-4, atol=1e-4)
+    np.testing.assert_allclose(std ** 2, var, rtol=1e-4, atol=1e-5)
+    m_l, s_l = gp.predict(Xs, return_std=True, variance_method="love")
+    np.testing.assert_allclose(m_l, mu, rtol=1e-4, atol=1e-4)
+    np.testing.assert_allclose(s_l ** 2, var, rtol=1e-4, atol=1e-5)
+    gp.save(str(tmp_path / "again.json"))
+    assert (tmp_path / "again_config.json").exists() and (tmp_path / "again_arrays.npz").exists()
+    gp2 = SingleOutputGP.load(str(tmp_path / "again"))
+    m2, s2 = gp2.predict(Xs, return_std=True, variance_method="love")
+    np.testing.assert_allclose(m2, m_l, rtol=1e-5, atol=1e-6)
+    np.testing.assert_allclose(s2, s_l, rtol=1e-5, atol=1e-6)
