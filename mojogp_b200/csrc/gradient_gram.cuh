@@ -33,6 +33,11 @@ constexpr int kGBUStages = 3;   // chunk stages in TMEM
 constexpr int kGBEpi = 128 * kGBRowTiles;
 constexpr int kGBThreads = kGBEpi + 32 * 3 * kGBRowTiles + 32;
 constexpr int kGBN = 80;        // MMA2 N: [B'hi | B'lo], 40 each (1 + 2 DP <= 40)
+// Accumulation window in column tiles: MMA2 restarts its accumulator every
+// kGBWinTiles tiles and the epilogue folds each finished window into its
+// per-row sums in fp32 registers, because the tensor core's accumulator
+// truncates toward zero on every add (see kGWinTiles).
+constexpr int kGBWinTiles = 4;
 constexpr uint32_t kGBColX = 0;                        // + 32 r
 constexpr uint32_t kGBColN = 32 * kGBRowTiles;         // + 8 r
 constexpr uint32_t kGBColA = kGBColN + 8 * kGBRowTiles;  // + 32 r : [a hi | a lo]
@@ -75,6 +80,7 @@ __global__ void __launch_bounds__(kGBThreads, 1) gb_kernel(
   __shared__ __align__(8) uint64_t afull_bar[kGBRowTiles][kGBUStages];
   __shared__ __align__(8) uint64_t m2_bar[kGBRowTiles][kGBUStages];
   __shared__ __align__(8) uint64_t final_bar[kGBRowTiles];
+  __shared__ __align__(8) uint64_t accfree_bar[kGBRowTiles];  // window folded
   __shared__ float red[kGBEpi / 32][NACC];
   __shared__ uint32_t tslot;
 
@@ -83,6 +89,7 @@ __global__ void __launch_bounds__(kGBThreads, 1) gb_kernel(
   const int t0 = split * tiles_per_split;
   const int ntiles = max(0, min(ntiles_total, t0 + tiles_per_split) - t0);
   const int G = ntiles * kChunks;
+  constexpr int kWin = kGBWinTiles * kChunks;  // chunks per accumulation window
   const uint32_t tile_bytes = TILE * sizeof(float);
   if (tid == 0) {
     for (int s = 0; s < kGBStages; ++s) {
@@ -96,6 +103,7 @@ __global__ void __launch_bounds__(kGBThreads, 1) gb_kernel(
         mbar_init(&m2_bar[r][s], 1);
       }
       mbar_init(&final_bar[r], 1);
+      mbar_init(&accfree_bar[r], 128);
     }
     fence_barrier_init();
   }
@@ -215,6 +223,10 @@ __global__ void __launch_bounds__(kGBThreads, 1) gb_kernel(
         const int st = g % kGBUStages;
         const int kt = g / kChunks, q = g % kChunks, slot = kt % kGBStages;
         if (q == 0) ok = mbar_wait_bounded(&full_bar[slot], (kt / kGBStages) & 1);
+        // A new window restarts the accumulator once the epilogue has folded
+        // the previous one.
+        if (ok && g > 0 && g % kWin == 0)
+          ok = mbar_wait_bounded(&accfree_bar[r], (g / kWin - 1) & 1);
         if (ok) ok = mbar_wait_bounded(&afull_bar[r][st], (g / kGBUStages) & 1);
         if (!ok) break;
         tc_fence_after();
@@ -222,7 +234,7 @@ __global__ void __launch_bounds__(kGBThreads, 1) gb_kernel(
 #pragma unroll
         for (int kk = 0; kk < 2; ++kk) {
           const uint64_t dbp = dp0 + off(slot * TILE + (2 * q + kk) * 8 * kGBN);
-          mma_tf32_tmem_a(acc, ae + kk * 8, dbp, idesc80, (g > 0 || kk > 0) ? 1u : 0u);
+          mma_tf32_tmem_a(acc, ae + kk * 8, dbp, idesc80, (g % kWin > 0 || kk > 0) ? 1u : 0u);
           mma_tf32_tmem_a(acc, ae + 16 + kk * 8, dbp, idesc48, 1u);
         }
         mma_commit(&m2_bar[r][st]);
@@ -235,6 +247,33 @@ __global__ void __launch_bounds__(kGBThreads, 1) gb_kernel(
     __syncwarp();
   } else {
     const uint32_t s_base = tmem + lane_off + kGBColS + rt * 96;
+    const uint32_t ab = tmem + lane_off + kGBColAcc + rt * kGBN;
+    // Per-row sums of the folded windows. The accumulators are linear in the
+    // pair terms, so each window's m0, m1, m2 are combined into the gradient
+    // sums right away.
+    float vals[NACC];
+#pragma unroll
+    for (int q = 0; q < NACC; ++q) vals[q] = 0.f;
+    auto fold = [&]() {
+      float acc[kGBN];
+#pragma unroll
+      for (int c = 0; c < kGBN; c += 16) {
+        float tmp[16];
+        tmem_ld16(ab + c, tmp);
+#pragma unroll
+        for (int h = 0; h < 16; ++h) acc[c + h] = tmp[h];
+      }
+      if (i < nrow) {
+        const float m0 = acc[0] + acc[40];
+#pragma unroll
+        for (int k = 0; k < DP; ++k) {
+          const float m1 = acc[1 + k] + acc[41 + k];
+          const float m2 = acc[1 + DP + k] + acc[41 + DP + k];
+          vals[k] += fmaf(x[k] * x[k], m0, fmaf(-2.f * x[k], m1, m2)) * (2.f * kLn2);
+        }
+        vals[DP] += m0;
+      }
+    };
     bool ok = true;
     for (int g = 0; g < G && ok; ++g) {
       const int st = g % kGBUStages;
@@ -257,34 +296,26 @@ __global__ void __launch_bounds__(kGBThreads, 1) gb_kernel(
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(&afull_bar[rt][st]);
+      if (g % kWin == 0 && g > 0) {
+        // First chunk of a window: fold the previous window once its last
+        // MMA2 has completed (after this chunk's work, hiding the latency).
+        const int gp = g - 1;
+        ok = mbar_wait_bounded(&m2_bar[rt][gp % kGBUStages], (gp / kGBUStages) & 1);
+        if (!ok) break;
+        tc_fence_after();
+        fold();
+        tc_fence_before();
+        mbar_arrive(&accfree_bar[rt]);
+      }
     }
     if (ok) ok = mbar_wait_bounded(&final_bar[rt], 0);
     tc_fence_after();
-    float vals[NACC];
-#pragma unroll
-    for (int q = 0; q < NACC; ++q) vals[q] = 0.f;
     if (!ok) {
       atomicExch(err, DEV_WAIT_TIMEOUT);
+#pragma unroll
+      for (int q = 0; q < NACC; ++q) vals[q] = 0.f;
     } else if (G > 0) {
-      float acc[kGBN];
-      const uint32_t ab = tmem + lane_off + kGBColAcc + rt * kGBN;
-#pragma unroll
-      for (int c = 0; c < kGBN; c += 16) {
-        float tmp[16];
-        tmem_ld16(ab + c, tmp);
-#pragma unroll
-        for (int h = 0; h < 16; ++h) acc[c + h] = tmp[h];
-      }
-      if (i < nrow) {
-        const float m0 = acc[0] + acc[40];
-#pragma unroll
-        for (int k = 0; k < DP; ++k) {
-          const float m1 = acc[1 + k] + acc[41 + k];
-          const float m2 = acc[1 + DP + k] + acc[41 + DP + k];
-          vals[k] = fmaf(x[k] * x[k], m0, fmaf(-2.f * x[k], m1, m2)) * (2.f * kLn2);
-        }
-        vals[DP] = m0;
-      }
+      fold();  // the last window
     }
     // Fixed-order reduction over the CTA's rows.
 #pragma unroll

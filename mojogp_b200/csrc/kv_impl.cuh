@@ -203,7 +203,8 @@ int kv_launch_impl(const KvLaunch& L) {
       return kv_tile_kernel<DP, T, R, kKvBlock, Ev>;
     }
   }();
-  const size_t smem = (size_t)S * kJT * W * sizeof(float);
+  // Ring stages plus the per-thread fold slots (R * T floats per thread).
+  const size_t smem = (size_t)S * kJT * W * sizeof(float) + (size_t)R * T * kKvBlock * sizeof(float);
 
   int dev = 0;
   GPB_CHECK_CUDA(cudaGetDevice(&dev));

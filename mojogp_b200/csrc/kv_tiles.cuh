@@ -149,6 +149,7 @@ __global__ void __launch_bounds__(BLK) kv_tile_kernel(const float* __restrict__ 
   const int t0 = split * tiles_per_split;
   const int ntiles = max(0, min(ntiles_total, t0 + tiles_per_split) - t0);
   TileRing ring{smem, bars, xv, t0, ntiles, (uint32_t)(kJT * W)};
+  float* tot = smem + kStages * kJT * W;  // [R * T][BLK] per-tile fold
   ring.start();
 
   // Row registers.
@@ -223,6 +224,23 @@ __global__ void __launch_bounds__(BLK) kv_tile_kernel(const float* __restrict__ 
         for (int c = 0; c < T; ++c) acc[r][c] = fmaf(kv[r], vj[c], acc[r][c]);
     }
     ring.release(kt);
+    // Fold this tile's sums into the running totals (shared memory, one slot
+    // per thread, row and column): no fp32 sum runs over more than one tile,
+    // where a flat sum over 1e6 columns drifts by up to ~u * sqrt(n).
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+#pragma unroll
+      for (int c = 0; c < T; ++c) {
+        float* slot = tot + (r * T + c) * BLK + tid;
+        *slot = (kt == 0 ? 0.f : *slot) + acc[r][c];
+        acc[r][c] = 0.f;
+      }
+  }
+  if (ntiles > 0) {
+#pragma unroll
+    for (int r = 0; r < R; ++r)
+#pragma unroll
+      for (int c = 0; c < T; ++c) acc[r][c] = tot[(r * T + c) * BLK + tid];
   }
 
   const bool partial = gridDim.y > 1;

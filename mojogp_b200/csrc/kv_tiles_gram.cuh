@@ -67,6 +67,16 @@ constexpr int kGChunk = 16;
 constexpr int kGStages = 4;    // column-tile ring depth (also keeps one CTA per SM)
 constexpr int kGUStages = GPB_GRAM_S;  // chunk stages in TMEM per row tile
 constexpr int kGPar = GPB_GRAM_P;      // issuer warps per role and row tile (chunk c -> c % kGPar)
+// Accumulation window, in column tiles. The tensor core adds into its fp32
+// accumulator with truncation (round toward zero), so a long run of MMAs into
+// one accumulator drifts toward zero by up to an ulp of the running sum per
+// MMA: over the 6e4 MMAs of a 1e6-column row that is ~1e-3 relative. Each
+// window of kGWinTiles tiles starts a fresh accumulator; the epilogue threads
+// fold the finished window into an fp32 register sum (round to nearest).
+#ifndef GPB_GRAM_WIN
+#define GPB_GRAM_WIN 4
+#endif
+constexpr int kGWinTiles = GPB_GRAM_WIN;
 constexpr int kGEpiThreads = 128 * kGRowTiles;
 constexpr int kGIssuerWarps = 2 * kGPar * kGRowTiles;  // MMA1 and MMA2 issuers
 constexpr int kGThreads = kGEpiThreads + 32 * kGIssuerWarps + 32;
@@ -134,6 +144,7 @@ __global__ void __launch_bounds__(kGThreads, 1) kv_tile_gram_kernel(
   __shared__ __align__(8) uint64_t d1_bar[kGRowTiles][kGUStages];     // MMA1 of a chunk done
   __shared__ __align__(8) uint64_t afull_bar[kGRowTiles][kGUStages];  // K hi / lo in TMEM
   __shared__ __align__(8) uint64_t m2_bar[kGRowTiles][kGUStages];     // MMA2 of a chunk done
+  __shared__ __align__(8) uint64_t accfree_bar[kGRowTiles][kGPar];    // window sum folded
   __shared__ __align__(8) uint64_t final_bar;
   __shared__ uint32_t tslot;
 
@@ -143,6 +154,9 @@ __global__ void __launch_bounds__(kGThreads, 1) kv_tile_gram_kernel(
   const int t0 = split * tiles_per_split;
   const int ntiles = max(0, min(ntiles_total, t0 + tiles_per_split) - t0);
   const int G = ntiles * kChunks;
+  constexpr int kWin = kGWinTiles * kChunks;  // chunks per accumulation window
+  static_assert(kWin % kGPar == 0, "every window starts on chunk class 0");
+  const int nwin = (G + kWin - 1) / kWin;
   const uint32_t tile_bytes = TILE * sizeof(float);
 
   if (tid == 0) {
@@ -156,6 +170,8 @@ __global__ void __launch_bounds__(kGThreads, 1) kv_tile_gram_kernel(
         mbar_init(&afull_bar[r][s], 128);
         mbar_init(&m2_bar[r][s], 1);
       }
+    for (int r = 0; r < kGRowTiles; ++r)
+      for (int p = 0; p < kGPar; ++p) mbar_init(&accfree_bar[r][p], 128);
     mbar_init(&final_bar, kGPar * kGRowTiles);
     fence_barrier_init();
   }
@@ -273,6 +289,14 @@ __global__ void __launch_bounds__(kGThreads, 1) kv_tile_gram_kernel(
         // V is read by this thread's MMAs: observe the TMA completion here too.
         if (q < kGPar) ok = mbar_wait_bounded(&full_bar[slot], (kt / kGStages) & 1);
         if (!ok) break;
+        // A new window restarts the accumulator once the epilogue has folded
+        // the previous window's value.
+        const int w = g / kWin;
+        if (w > 0 && g % kWin == par) {
+          ok = mbar_wait_bounded(&accfree_bar[r][par], (w - 1) & 1);
+          if (!ok) break;
+          first = true;
+        }
         GRAM_T0(aw);
         ok = mbar_wait_bounded(&afull_bar[r][st], (g / kGUStages) & 1);
         GRAM_ACC(6, aw);
@@ -301,6 +325,9 @@ __global__ void __launch_bounds__(kGThreads, 1) kv_tile_gram_kernel(
   } else {
     const uint32_t s_base = tmem + lane_off + kGColS + rt * 32 * kGUStages;
     const uint32_t acc_col = tmem + lane_off + kGColAcc + rt * 16 * kGPar;
+    float wsum[16];  // finished accumulation windows (fp32, round to nearest)
+#pragma unroll
+    for (int c = 0; c < 16; ++c) wsum[c] = 0.f;
     bool ok = true;
     GRAM_T0(etot);
     for (int g = 0; g < G && ok; ++g) {
@@ -328,6 +355,29 @@ __global__ void __launch_bounds__(kGThreads, 1) kv_tile_gram_kernel(
       tmem_wait_st();
       tc_fence_before();
       mbar_arrive(&afull_bar[rt][st]);
+      if (g % kWin == 0 && g > 0) {
+        // First chunk of a window: fold the previous window once its last
+        // MMA2 of each chunk class has completed, and free the accumulators.
+        // Doing it after this chunk's exponentials (not at the window's last
+        // chunk) hides the MMA2 latency behind them.
+#pragma unroll
+        for (int p = 0; p < kGPar && ok; ++p) {
+          const int gp = g - kGPar + p;
+          ok = mbar_wait_bounded(&m2_bar[rt][gp % kGUStages], (gp / kGUStages) & 1);
+        }
+        if (!ok) break;
+        tc_fence_after();
+#pragma unroll
+        for (int p = 0; p < kGPar; ++p) {
+          float a[16];
+          tmem_ld16(acc_col + 16 * p, a);
+#pragma unroll
+          for (int c = 0; c < 16; ++c) wsum[c] += a[c];
+        }
+        tc_fence_before();
+#pragma unroll
+        for (int p = 0; p < kGPar; ++p) mbar_arrive(&accfree_bar[rt][p]);
+      }
     }
     GRAM_ACC(1, etot);
     if (ok) ok = mbar_wait_bounded(&final_bar, 0);
@@ -335,19 +385,21 @@ __global__ void __launch_bounds__(kGThreads, 1) kv_tile_gram_kernel(
     if (!ok) {
       atomicExch(err, DEV_WAIT_TIMEOUT);
     } else {
+      // The last window's accumulators, for the chunk classes that had a
+      // chunk in it (a class without one still holds a folded window).
       float acc[16];
-      if (G > 0) {
-        tmem_ld16(acc_col, acc);  // chunk class 0
-        for (int p = 1; p < kGPar && p < G; ++p) {
-          float acc_p[16];
-          tmem_ld16(acc_col + 16 * p, acc_p);
 #pragma unroll
-          for (int c = 0; c < 16; ++c) acc[c] += acc_p[c];
-        }
-      } else {
+      for (int c = 0; c < 16; ++c) acc[c] = 0.f;
+      const int last0 = (nwin - 1) * kWin;
+      for (int p = 0; p < kGPar && G > 0; ++p) {
+        if (last0 + p >= G) break;
+        float acc_p[16];
+        tmem_ld16(acc_col + 16 * p, acc_p);
 #pragma unroll
-        for (int c = 0; c < 16; ++c) acc[c] = 0.f;
+        for (int c = 0; c < 16; ++c) acc[c] += acc_p[c];
       }
+#pragma unroll
+      for (int c = 0; c < 16; ++c) acc[c] += wsum[c];
       const bool partial = gridDim.y > 1;
       if (i < nrow) {
 #pragma unroll
@@ -535,9 +587,12 @@ __global__ void __launch_bounds__(kG1Threads, 1) kv_tile_gram1_kernel(
     __syncwarp();
   } else {
     const uint32_t s_base = tmem + lane_off + kG1ColS + rt * kG1UStages * 16;
-    float acc[NV];
+    // Two-level fp32 sum: a running sum per column tile, folded into the
+    // total once per tile, so no sum runs over more than 128 columns
+    // (a flat fp32 sum over 1e6 columns drifts by ~u * sqrt(n) ~ 6e-5).
+    float acc[NV], tot[NV];
 #pragma unroll
-    for (int c = 0; c < NV; ++c) acc[c] = 0.f;
+    for (int c = 0; c < NV; ++c) acc[c] = tot[c] = 0.f;
     bool ok = true;
     for (int g = 0; g < G && ok; ++g) {
       const int st = g % kG1UStages;
@@ -562,8 +617,15 @@ __global__ void __launch_bounds__(kG1Threads, 1) kv_tile_gram1_kernel(
       if (q == kChunks - 1) {
         __syncwarp();
         if (lane == 0) mbar_arrive(&tile_bar[slot]);
+#pragma unroll
+        for (int c = 0; c < NV; ++c) {
+          tot[c] += acc[c];
+          acc[c] = 0.f;
+        }
       }
     }
+#pragma unroll
+    for (int c = 0; c < NV; ++c) acc[c] += tot[c];
     if (!ok) {
       atomicExch(err, DEV_WAIT_TIMEOUT);
     } else if (i < nrow) {

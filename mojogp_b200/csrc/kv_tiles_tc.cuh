@@ -29,6 +29,15 @@ constexpr int kTcChunk = 8;        // columns per K block (one MMA k-step)
 constexpr int kTcRows = 4;         // row tiles (M = 128 each) per CTA
 constexpr int kTcThreads = 128;
 constexpr int kTcAStageBytes = kTcRows * 2 * 128 * kTcChunk * 4;  // hi + lo, both row tiles
+// Accumulation window in column tiles. The tensor core's fp32 accumulator
+// truncates toward zero on every add, so a chain of MMAs over a 1e6-column
+// row drifts by ~1e-3 relative. The MMAs of window w accumulate into TMEM
+// set w % 2 from zero; while window w runs, the row threads fold window
+// w - 1's set into a TMEM sum (fp32, round to nearest). TMEM: [set 0 | set 1 |
+// sum], 16 columns per row tile each.
+constexpr int kTcWinTiles = 4;
+constexpr uint32_t kTcTmemCols = 256;
+static_assert(3 * 16 * kTcRows <= kTcTmemCols, "TMEM budget");
 
 // Packed tile: [-x' : 128 x DP][V hi : 16 k-steps x 128][V lo : 16 k-steps x 128] floats.
 __host__ __device__ constexpr int tc_tile_floats(int DP) { return 128 * DP + 2 * 16 * 128; }
@@ -68,6 +77,8 @@ __global__ void __launch_bounds__(kTcThreads + 32, 2) kv_tile_tc_kernel(
   const int t0 = split * tiles_per_split;
   const int ntiles = max(0, min(ntiles_total, t0 + tiles_per_split) - t0);
   constexpr int kChunks = 128 / kTcChunk;
+  constexpr int kWin = kTcWinTiles * kChunks;  // chunks per accumulation window
+  constexpr uint32_t kSumCol = 2 * 16 * kTcRows;
 
   if (tid == 0) {
     for (int s = 0; s < kTcStages; ++s) {
@@ -81,7 +92,7 @@ __global__ void __launch_bounds__(kTcThreads + 32, 2) kv_tile_tc_kernel(
     abort_flag = 0;
     fence_barrier_init();
   }
-  if (warp == 4) tmem_alloc(&tslot, 16 * kTcRows);  // power of two >= 32
+  if (warp == 4) tmem_alloc(&tslot, kTcTmemCols);  // two CTAs per SM share the 512 columns
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
@@ -115,13 +126,13 @@ __global__ void __launch_bounds__(kTcThreads + 32, 2) kv_tile_tc_kernel(
           for (int r = 0; r < kTcRows; ++r) {
             const float* ahi = ablk + r * 2 * (128 * kTcChunk);
             const float* alo = ahi + 128 * kTcChunk;
-            const uint32_t d = tmem + r * 16;
+            const uint32_t d = tmem + ((g / kWin) & 1) * (16 * kTcRows) + r * 16;
             static_assert(kTcChunk == 8, "one MMA k-step per K block");
             const uint64_t dah = make_smem_desc(ahi, 2048, 128);
             const uint64_t dal = make_smem_desc(alo, 2048, 128);
             const uint64_t dbh = make_smem_desc(bhi + q * 128, 256, 128);
             const uint64_t dbl = make_smem_desc(blo + q * 128, 256, 128);
-            mma_tf32(d, dah, dbh, idesc, g > 0 ? 1u : 0u);
+            mma_tf32(d, dah, dbh, idesc, g % kWin > 0 ? 1u : 0u);
             mma_tf32(d, dah, dbl, idesc, 1u);
             mma_tf32(d, dal, dbh, idesc, 1u);
           }
@@ -158,6 +169,26 @@ __global__ void __launch_bounds__(kTcThreads + 32, 2) kv_tile_tc_kernel(
         xi[rp][k] = make_float2(i0 < nrow ? xrow[i0 * DP + k] : 0.f, i1 < nrow ? xrow[i1 * DP + k] : 0.f);
     }
     const int a_row_off = (tid / 8) * 32 + (tid % 8) * 4;
+    const uint32_t lane_sel = (uint32_t)(warp * 32) << 16;
+    // sum (+)= accumulator set at `set_col`, for this thread's rows of every row tile.
+    auto fold_set = [&](uint32_t set_col, bool add) {
+#pragma unroll 1
+      for (int r = 0; r < kTcRows; ++r) {
+        float a[16];
+        tmem_ld16(set_col + lane_sel + r * 16, a);
+        if (add) {
+          float s[16];
+          tmem_ld16(tmem + lane_sel + kSumCol + r * 16, s);
+#pragma unroll
+          for (int c = 0; c < 16; ++c) a[c] += s[c];
+        }
+        uint32_t b[16];
+#pragma unroll
+        for (int c = 0; c < 16; ++c) b[c] = __float_as_uint(a[c]);
+        tmem_st16(tmem + lane_sel + kSumCol + r * 16, b);
+      }
+      tmem_wait_st();
+    };
     int g = 0;
     bool ok = true;
     for (int kt = 0; kt < ntiles && ok; ++kt) {
@@ -171,6 +202,13 @@ __global__ void __launch_bounds__(kTcThreads + 32, 2) kv_tile_tc_kernel(
           ok = mbar_wait_bounded(&mma_bar[st], ((g - 2) >> 1) & 1);
           if (!ok) break;
           tc_fence_after();
+        }
+        if (g % kWin == 1 && g > kWin) {
+          // The MMAs of chunk g - 2, the last of window w - 1, are complete
+          // (and with them all earlier ones): fold that window's set into the
+          // sum. Window w + 1 reuses the set only after this chunk's arrival.
+          const int w1 = g / kWin - 1;
+          fold_set(tmem + (uint32_t)(w1 & 1) * (16 * kTcRows), w1 > 0);
         }
         float* ablk = abuf + st * (kTcAStageBytes / 4);
 #pragma unroll
@@ -216,6 +254,7 @@ __global__ void __launch_bounds__(kTcThreads + 32, 2) kv_tile_tc_kernel(
           }
         }
         fence_proxy_async_smem();
+        tc_fence_before();
         mbar_arrive(&afull_bar[st]);
       }
       if (!ok) break;
@@ -228,14 +267,23 @@ __global__ void __launch_bounds__(kTcThreads + 32, 2) kv_tile_tc_kernel(
       atomicExch(err, DEV_WAIT_TIMEOUT);
     } else {
       const bool partial = gridDim.y > 1;
-#pragma unroll
+      // Windows folded during the loop: 0 .. folded - 1 (window w - 1 is
+      // folded at chunk w * kWin + 1). The rest (one or two) are added here.
+      const int nwin = (g + kWin - 1) / kWin;
+      int folded = 0;
+      for (int w = 1; w < nwin; ++w)
+        if (w * kWin + 1 < g) folded = w;
+#pragma unroll 1
       for (int r = 0; r < kTcRows; ++r) {
         float acc[16];
-        if (g > 0) {
-          tmem_ld16(tmem + r * 16 + ((uint32_t)(warp * 32) << 16), acc);
-        } else {
 #pragma unroll
-          for (int c = 0; c < 16; ++c) acc[c] = 0.f;
+        for (int c = 0; c < 16; ++c) acc[c] = 0.f;
+        if (folded > 0) tmem_ld16(tmem + lane_sel + kSumCol + r * 16, acc);
+        for (int w = folded; w < nwin; ++w) {
+          float a[16];
+          tmem_ld16(tmem + lane_sel + (uint32_t)(w & 1) * (16 * kTcRows) + r * 16, a);
+#pragma unroll
+          for (int c = 0; c < 16; ++c) acc[c] += a[c];
         }
         const int64_t i = row0 + (int64_t)r * 128;
         if (i < nrow) {
@@ -259,7 +307,7 @@ __global__ void __launch_bounds__(kTcThreads + 32, 2) kv_tile_tc_kernel(
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 4) tmem_dealloc(tmem, 16 * kTcRows);
+  if (warp == 4) tmem_dealloc(tmem, kTcTmemCols);
 }
 
 }  // namespace gpb

@@ -31,6 +31,7 @@ __global__ void __launch_bounds__(BLK) kv_tile_x2_kernel(const float* __restrict
   const int t0 = split * tiles_per_split;
   const int ntiles = max(0, min(ntiles_total, t0 + tiles_per_split) - t0);
   TileRingT<kStagesX2> ring{smem, bars, xv, t0, ntiles, (uint32_t)(kJT * W)};
+  float2* tot = reinterpret_cast<float2*>(smem + kStagesX2 * kJT * W);  // [RP * T][BLK]
   ring.start();
 
   const int64_t row0 = (int64_t)blockIdx.x * (BLK * R) + tid;
@@ -91,6 +92,23 @@ __global__ void __launch_bounds__(BLK) kv_tile_x2_kernel(const float* __restrict
       }
     }
     ring.release(kt);
+    // Fold this tile's sums into the running totals in shared memory (see
+    // kv_tile_kernel).
+#pragma unroll
+    for (int q = 0; q < RP; ++q)
+#pragma unroll
+      for (int c = 0; c < T; ++c) {
+        float2* slot = tot + (q * T + c) * BLK + tid;
+        const float2 prev = kt == 0 ? make_float2(0.f, 0.f) : *slot;
+        *slot = __fadd2_rn(prev, acc[q][c]);
+        acc[q][c] = make_float2(0.f, 0.f);
+      }
+  }
+  if (ntiles > 0) {
+#pragma unroll
+    for (int q = 0; q < RP; ++q)
+#pragma unroll
+      for (int c = 0; c < T; ++c) acc[q][c] = tot[(q * T + c) * BLK + tid];
   }
 
   const bool partial = gridDim.y > 1;

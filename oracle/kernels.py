@@ -250,3 +250,24 @@ def gradient_bilinear(spec, params, X, A, B):
     data = np.array([A[:, 0] @ g @ B[:, 0] for g in G])
     trace = np.array([sum(A[:, c] @ g @ B[:, c] for c in range(1, A.shape[1])) for g in G])
     return data, trace
+
+
+def gradient_bilinear_rows(spec, params, X, rows, A_rows, B, block=4):
+    """gradient_bilinear restricted to rows: with a_i = 0 outside `rows`,
+    data[p] = sum_{i in rows} a_i0 dK_p[i, :] b_0 and likewise trace over
+    columns c >= 1. A_rows [len(rows), t] holds the nonzero rows of A. Row
+    blocks keep memory at block x n x dims, so rows against 1e6 columns fit."""
+    X = np.asarray(X, np.float64)
+    B = np.asarray(B, np.float64)
+    A_rows = np.asarray(A_rows, np.float64)
+    rows = np.asarray(rows)
+    data = trace = None
+    for b0 in range(0, len(rows), block):
+        r = rows[b0:b0 + block]
+        _, G = kernel_matrix(spec, params, X[r], X, want_grad=True)
+        a = A_rows[b0:b0 + block]
+        d = np.array([a[:, 0] @ (g @ B[:, 0]) for g in G])
+        t = np.array([np.sum(a[:, 1:] * (g @ B[:, 1:])) for g in G])
+        data = d if data is None else data + d
+        trace = t if trace is None else trace + t
+    return data, trace

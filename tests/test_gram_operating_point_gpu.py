@@ -146,3 +146,35 @@ def test_gb_kernel_near_gate(gpb_lib):
     k = make_ard_kernel(RBF(ard=True), d)
     p = _params(k, d, ell, rng)
     _check_bilinear(X, k, p, d, rng)
+
+
+def test_gb_kernel_config3_full_columns(gpb_lib):
+    """The fused RBF gradient reduction over all 1e6 columns of config 3
+    (every row's sum runs the full column range, where an unwindowed
+    tensor-core accumulator would drift), with A zero outside 32 rows (the
+    16 largest |x'|^2 and 16 random) so the float64 oracle can follow it."""
+    X, _, ell = synthetic.config3()
+    n, d, t = X.shape[0], X.shape[1], 16
+    sq = _sqnorm(X, ell, "rbf")
+    rng = np.random.default_rng(13)
+    rows = np.unique(np.concatenate([np.argsort(sq)[-16:], rng.choice(n, 16, replace=False)]))
+    k = make_ard_kernel(RBF(ard=True), d)
+    p = np.concatenate([ell, [1.0]]).astype(np.float32)
+    prov = Provider(X, k, p, 0.0025)
+    assert prov.matvec_layout(16) == "gram-tensor-core"
+    A = np.zeros((t, n), np.float32)
+    A[:, rows] = rng.standard_normal((t, len(rows))).astype(np.float32)
+    B = rng.standard_normal((t, n)).astype(np.float32)
+    ad, bd = DeviceBuffer.from_host(A), DeviceBuffer.from_host(B)
+    data, trace = prov.gradient_bilinear(ad, bd, t)
+    spec = k.to_spec(d)
+
+    def part(r):
+        return ok.gradient_bilinear_rows(spec, p, X, r, A[:, r].T, B.T, block=2)
+
+    with cf.ThreadPoolExecutor(min(8, os.cpu_count() or 1)) as ex:
+        parts = list(ex.map(part, np.array_split(rows, 8)))
+    rd = sum(q[0] for q in parts)
+    rt = sum(q[1] for q in parts)
+    np.testing.assert_allclose(data, rd, rtol=1e-4, atol=1e-4 * np.abs(rd).max())
+    np.testing.assert_allclose(trace, rt, rtol=1e-4, atol=1e-4 * np.abs(rt).max())
