@@ -768,17 +768,20 @@ class MultiOutputGP(_ObservedPredictionMixin):
             B = W @ W.T + np.diag([_sp(r) for r in raw_v])
             self._lmc.set_coregion((os_ * B)[None].astype(np.float32), noise)
             state = (np.concatenate([params, [os_], noise, B.ravel()]))
-            if self.precond_rank > 0:
-                rebuild = last is None or np.max(np.abs(state - last) /
-                                                 (np.abs(last) + 1e-8)) > self.precond_rebuild_threshold
-                if rebuild:
-                    if last is not None:
-                        self.precond_rebuild_count += 1
+            # The rebuild rule (jit_multi_output.mojo:336-379) runs with or
+            # without a preconditioner; a rebuild iteration does not recycle
+            # the previous solution (:398-403).
+            rebuild = last is None or np.max(np.abs(state - last) /
+                                             (np.abs(last) + 1e-8)) > self.precond_rebuild_threshold
+            if rebuild:
+                if last is not None:
+                    self.precond_rebuild_count += 1
+                if self.precond_rank > 0:
                     self._lmc.build_precond(self.precond_rank)
-                    last = state
+                last = state
             yc = (Yb - raw_mean[:, None]).astype(np.float32)
             res = self._lmc.bbmm(yc, self.num_probes, self.max_cg_iter, self.max_tridiag_iter,
-                                 self.cg_tol, it, it > 0)
+                                 self.cg_tol, it, it > 0 and not rebuild)
             if res["cg_iters"] >= self.max_cg_iter and self.precond_rank > 0:
                 # jit_multi_output.mojo: rebuild the preconditioner and retry once
                 self._lmc.build_precond(self.precond_rank)
@@ -810,10 +813,11 @@ class MultiOutputGP(_ObservedPredictionMixin):
             for t in range(T):
                 raw_noise[t] += adam(idx, res["gnoise"][t] * sig(raw_noise[t]))
                 idx += 1
-            gW = 2.0 * G_B @ W
+            # Row by row in place: each row's gradient reads the rows already
+            # updated in this iteration (jit_multi_output.mojo:648-662).
             for s in range(T):
                 for r in range(R):
-                    W[s, r] += adam(idx, gW[s, r])
+                    W[s, r] += adam(idx, 2.0 * float(G_B[s, :] @ W[:, r]))
                     idx += 1
             for t in range(T):
                 raw_v[t] += adam(idx, G_B[t, t] * sig(raw_v[t]))

@@ -97,8 +97,12 @@ class LmcPrecond:
 
 
 def lmc_bbmm(specs, params_list, X, Y_centered, A, noise, num_probes, max_cg, max_tridiag, tol,
-             iteration=0, precond_rank=0):
-    """Y_centered [n, T]. Returns nll, kernel grads (concatenated), grad_A, grad_noise."""
+             iteration=0, precond_rank=0, precond=None, x_prev=None):
+    """Y_centered [n, T]. Returns nll, kernel grads (concatenated), grad_A, grad_noise.
+    `precond` (an LmcPrecond) is used as given, e.g. one built at an earlier
+    state; else precond_rank > 0 builds one here. `x_prev` starts the data
+    column's CG from a previous normalised solution (recycle_alpha,
+    combined_inv_quad_logdet.mojo); the result's x_norm0 is this solve's."""
     X = np.asarray(X, np.float64)
     n = X.shape[0]
     A = np.asarray(A, np.float64)
@@ -107,12 +111,17 @@ def lmc_bbmm(specs, params_list, X, Y_centered, A, noise, num_probes, max_cg, ma
     y = np.asarray(Y_centered, np.float64).T.reshape(nT)  # task-blocked
     K, Ks, Gs = full_operator(specs, params_list, X, A, np.asarray(noise, np.float64))
     seed = iteration * 104729 + 42
-    P = LmcPrecond(Ks, A, noise, precond_rank) if precond_rank > 0 else None
+    P = precond if precond is not None else \
+        (LmcPrecond(Ks, A, noise, precond_rank) if precond_rank > 0 else None)
     Z = P.sample(num_probes, seed) if P is not None else ob.gaussian_block(nT, num_probes, seed)
     pn = np.linalg.norm(Z, axis=0)
     rhs = np.concatenate([y[:, None], Z / pn], axis=1)
     rn = np.linalg.norm(rhs, axis=0)
-    x, iters, dg, od = ob.mbcg(K, rhs / rn, max_cg, max_tridiag, tol, P)
+    x0 = None
+    if x_prev is not None:
+        x0 = np.zeros_like(rhs)
+        x0[:, 0] = x_prev
+    x, iters, dg, od = ob.mbcg(K, rhs / rn, max_cg, max_tridiag, tol, P, x0)
     W = P.apply(Z) if P is not None else Z  # right factors
     sol = x * rn
     alpha = sol[:, 0]
@@ -139,4 +148,5 @@ def lmc_bbmm(specs, params_list, X, Y_centered, A, noise, num_probes, max_cg, ma
                           / num_probes) / nT for t in range(T)])
     sum_alpha = np.array([blk(alpha, t).sum() for t in range(T)])
     return {"nll": nll, "kgrads": np.array(kgrads), "gA": gA, "gnoise": gn,
-            "sum_alpha": sum_alpha, "cg_iters": iters, "K": K}
+            "sum_alpha": sum_alpha, "cg_iters": iters, "K": K, "Ks": Ks, "alpha": alpha,
+            "x_norm0": x[:, 0]}
