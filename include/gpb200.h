@@ -189,6 +189,14 @@ int gpb_comm_destroy(gpb_comm* c);
 int gpb_comm_allreduce_max_f64(gpb_comm* c, double* value_inout);
 int gpb_comm_allreduce_sum_f64(gpb_comm* c, double* values_inout, int64_t count);
 int gpb_comm_barrier(gpb_comm* c);
+/* One row-sharded (K + noise I) V product, as every mBCG iteration runs it
+ * (no reference counterpart; the reference is single-GPU): each rank passes
+ * its rows [n*rank/world, n*(rank+1)/world) of the ncols columns
+ * (v_local_dev [ncols][n_local]) and receives the same rows of the product
+ * (out_local_dev [ncols][n_local]); the column side is all-gathered over
+ * NCCL. comm NULL = one GPU (n_local = n). */
+int gpb_matvec_sharded(gpb_provider* p, gpb_comm* comm, float* out_local_dev,
+                       const float* v_local_dev, int64_t ncols);
 /* Row-sharded forward matvec benchmark: each rank computes rows
  * [n*rank/world, n*(rank+1)/world) of (K + noise) V and all-gathers the packed
  * output blocks, i.e. one CG-iteration matvec. Same outputs as

@@ -65,6 +65,7 @@ SIGNATURES = {
     "gpb_train": [P, P, P, c_i64, P, P],
     "gpb_bbmm": [P, P, P, c_i64, c_i32, c_i32, c_i32, c_f32, c_i32, c_i32, P, P, P, P, P],
     "gpb_precond_pivots": [P, P, c_i32, P, P, PI32],
+    "gpb_matvec_sharded": [P, P, P, P, c_i64],
     "gpb_slq_logdet": [P, P, c_i32, c_i32, c_i64, P],
     "gpb_tridiag_eig": [P, P, c_i32, P, P],
     "gpb_hash_gaussian": [c_i32, P, c_i64, C.c_uint64],

@@ -682,6 +682,22 @@ int gpb_precond_pivots(gpb_provider* p, gpb_comm* comm, int32_t rank, int64_t* p
   return provider_check_device_error(p);
 }
 
+int gpb_matvec_sharded(gpb_provider* p, gpb_comm* comm, float* out_local_dev,
+                       const float* v_local_dev, int64_t ncols) {
+  clear_error();
+  GPB_REQUIRE(p && out_local_dev && v_local_dev && ncols >= 1, GPB_ERR_INVALID, "bad arguments");
+  GPB_CHECK_CUDA(cudaSetDevice(p->device));
+  Engine E;
+  GPB_TRY(engine_from_comm(p, comm, E));
+  // Engine::matvec packs from its column argument, so stage the caller's
+  // (read-only) block in a local copy.
+  DBuf vloc;
+  GPB_TRY(vloc.ensure(E.blk((int)ncols) + 16));
+  GPB_TRY(k_copy(vloc.f(), v_local_dev, (int64_t)ncols * E.nl, E.st));
+  GPB_TRY(E.matvec(vloc.f(), E.nl, (int)ncols, out_local_dev, E.nl));
+  return provider_check_device_error(p);
+}
+
 int gpb_benchmark_forward_sharded(gpb_provider* p, gpb_comm* c, const float* v_dev, int64_t ncols,
                                   int32_t warmup, int32_t steps, int32_t flush_l2,
                                   double* step_ms_out, double* kernel_ms_out,

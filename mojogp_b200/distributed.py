@@ -122,6 +122,17 @@ class Communicator:
                   C.c_void_p(launches.ctypes.data))
         return step_ms, kern_ms, launches
 
+    def matvec_sharded(self, prov, V_local: np.ndarray) -> np.ndarray:
+        """(K + noise I) V for this rank's rows: V_local [t][n_local] host
+        array of this rank's rows, returns the same rows of the product (the
+        mBCG iteration's product, column side all-gathered over NCCL)."""
+        from .provider import DeviceBuffer
+        V_local = np.ascontiguousarray(V_local, np.float32)
+        vd = DeviceBuffer.from_host(V_local, prov.device)
+        od = DeviceBuffer(V_local.shape, prov.device)
+        _lib.call("gpb_matvec_sharded", prov.h, self.h, od.cptr, vd.cptr, V_local.shape[0])
+        return od.download()
+
     def e2e_sharded(self, prov, Vc: np.ndarray, t: int, r0: int, r1: int, flops_total: float,
                     reps: int = 2) -> float:
         """Host V in, this rank's output rows back to the host; max over ranks."""

@@ -75,6 +75,35 @@ def main(out_path):
         # Exact LMC variance through the sharded operator (every rank gets all).
         ev, _ = lmc.exact_variance(Xl[:25] + 0.03, 300, 1e-5)
         res[tag]["exact_var"] = ev.ravel().tolist()
+    # Greedy pivots with the argmax all-reduced over the ranks: the same list.
+    res["pivots"] = engine.precond_pivots(prov, 40, comm=comm)["pivots"].tolist()
+    # Config-3 recipe (X ~ N(0, I), d = 16, RBF-ARD on the Gram tensor-core
+    # path) at n = 2e5: one sharded mBCG product, this rank's rows checked
+    # on a row sample (its 32 largest |x'|^2 and 32 random rows) against the
+    # float64 oracle; rows of a fixed global sample are reported for the
+    # comparison with one GPU.
+    from mojogp_b200 import synthetic
+    from oracle import kernels as ok
+    Xc, _, ell = synthetic.config3(n=200_000)
+    nc, dc, t = Xc.shape[0], Xc.shape[1], 16
+    kc = make_ard_kernel(RBF(ard=True), dc)
+    pc = np.concatenate([ell, [1.0]]).astype(np.float32)
+    provc = Provider(Xc, kc, pc, 0.0025, device=comm.device)
+    V = np.random.default_rng(8).standard_normal((t, nc)).astype(np.float32)
+    r0, r1 = (rank * nc) // comm.world, ((rank + 1) * nc) // comm.world
+    out = comm.matvec_sharded(provc, V[:, r0:r1])
+    sq = 0.5 / np.log(2.0) * ((Xc[r0:r1].astype(np.float64) / ell) ** 2).sum(1)
+    local = np.unique(np.concatenate([np.argsort(sq)[-32:],
+                                      np.random.default_rng(rank).choice(r1 - r0, 32, replace=False)]))
+    ref = ok.forward_matvec(kc.to_spec(dc), pc, Xc, V.T, noise=0.0025, rows=local + r0, block=16)
+    got = out[:, local].T
+    mine = {"c3_err": float(np.linalg.norm(got - ref) / np.linalg.norm(ref)),
+            "c3_layout": provc.matvec_layout(16)}
+    fixed = np.random.default_rng(99).choice(nc, 64, replace=False)
+    own = fixed[(fixed >= r0) & (fixed < r1)]
+    mine["c3_rows"] = own.tolist()
+    mine["c3_vals"] = out[:, own - r0].T.tolist()
+    Path(f"{out_path}.r{rank}").write_text(json.dumps(mine))
     comm.barrier()
     if rank == 0:
         Path(out_path).write_text(json.dumps(res))

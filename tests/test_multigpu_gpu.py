@@ -35,7 +35,9 @@ def _run(nproc, out, tmp_path):
            str(out)]
     r = subprocess.run(cmd, env=env, capture_output=True, text=True, timeout=600)
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
-    return json.loads(Path(out).read_text())
+    res = json.loads(Path(out).read_text())
+    res["c3"] = [json.loads(Path(f"{out}.r{r}").read_text()) for r in range(nproc)]
+    return res
 
 
 def test_two_gpu_sharded_engine_matches_one_gpu(gpb_lib, tmp_path):
@@ -48,7 +50,9 @@ def test_two_gpu_sharded_engine_matches_one_gpu(gpb_lib, tmp_path):
                                atol=1e-3 * np.abs(one["bbmm_grads"]).max())
     np.testing.assert_allclose(two["train_nll"], one["train_nll"], rtol=1e-4)
     np.testing.assert_allclose(two["train_params"], one["train_params"], rtol=1e-4)
-    np.testing.assert_allclose(two["alpha_head"], one["alpha_head"], rtol=1e-3, atol=1e-4)
+    # alpha: CG to 1e-5 on a system of condition ~1e4 in float32 stalls near
+    # its rounding floor, so the two reduction orders differ by ~kappa * eps.
+    np.testing.assert_allclose(two["alpha_head"], one["alpha_head"], rtol=1e-3, atol=5e-4)
     np.testing.assert_allclose(two["mean"], one["mean"], rtol=1e-4, atol=1e-4)
     np.testing.assert_allclose(two["var"], one["var"], rtol=1e-3, atol=1e-5)
     np.testing.assert_allclose(two["mean_sharded"], one["mean"], rtol=1e-4, atol=1e-4)
@@ -67,3 +71,16 @@ def test_two_gpu_sharded_engine_matches_one_gpu(gpb_lib, tmp_path):
             if err >= 1e-3:
                 bad.append(f"{tag} {key} rel err {err:.2e}")
     assert not bad, "; ".join(bad)
+    # Pivot list of the sharded argmax: identical to one GPU.
+    assert two["pivots"] == one["pivots"]
+    # Config-3 recipe sharded product: every rank's row sample within the
+    # 1e-5 matvec bar of the float64 oracle, and the fixed rows equal to one GPU.
+    for part in one["c3"] + two["c3"]:
+        assert part["c3_layout"] == "gram-tensor-core"
+        assert part["c3_err"] < 1e-5, part["c3_err"]
+    def rows(parts):
+        return {r: v for p in parts for r, v in zip(p["c3_rows"], p["c3_vals"])}
+    a, b = rows(one["c3"]), rows(two["c3"])
+    assert sorted(a) == sorted(b)
+    for r in a:
+        np.testing.assert_allclose(b[r], a[r], rtol=1e-6, atol=1e-6)
