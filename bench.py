@@ -49,9 +49,11 @@ def parse():
     ap.add_argument("--rhs", dest="t", type=int, default=16)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-seconds", type=float, default=12.0)
-    ap.add_argument("--workload", default="c3", choices=["c1", "c2", "c3", "c3fit", "c4", "c5"],
+    ap.add_argument("--workload", default="c3", choices=["c1", "c2", "c3", "c3fit", "c4", "c5", "materialized"],
                     help="c3: the headline K·V / fit line (default); c3fit: the config-3 fit alone "
-                         "(--cfg-iters iterations, rows sharded); c1, c2, c4: the other "
+                         "(--cfg-iters iterations, rows sharded); materialized: matrix-free K·V "
+                         "against the reference's materialized route (dense K + SGEMM) at "
+                         "n = 4e4; c1, c2, c4: the other "
                          "fit configurations (1 GPU); c5: LOVE prediction at scale")
     ap.add_argument("--cfg-iters", type=int, default=50,
                     help="c1 / c2 / c4: outer fit iterations")
@@ -283,6 +285,84 @@ def run_c3fit(args, rank: int, world: int, local: int) -> None:
         comm.close()
 
 
+def run_materialized(args, rank: int, world: int, local: int) -> None:
+    """The reference's materialized route (fn_ptr_module.py:363-421: K filled
+    densely once per parameter update, then every product is an fp32 SGEMM
+    with use_tf32=False) against this library's matrix-free K·V at the size
+    that route serves (n = 4e4, RBF-ARD, t = 16). The dense side runs in torch
+    (fp32 cuBLAS, TF32 off) as the measurement of a plain library GEMM; both
+    sides are CUDA-event timed with inputs resident."""
+    if rank != 0:
+        return
+    import torch  # before the library: its NCCL must be the one loaded
+    import ctypes as C
+    from mojogp_b200 import _lib, synthetic
+    from mojogp_b200.kernel import RBF, make_ard_kernel
+    from mojogp_b200.provider import DeviceBuffer, Provider
+    torch.backends.cuda.matmul.allow_tf32 = False
+    n, d, t = (args.n if args.n != 1_000_000 else 40_000), 8, 16
+    X, _ = synthetic.config2(n=n, d=d)
+    ell = np.random.default_rng(4).uniform(0.5, 3.0, size=d).astype(np.float32)
+    params = np.concatenate([ell, [1.0]]).astype(np.float32)
+    prov = Provider(X, make_ard_kernel(RBF(ard=True), d), params, 0.01, device=local)
+    V = synthetic.probes_v(n, t, seed=1)
+    vd = DeviceBuffer.from_host(np.ascontiguousarray(V.T), local)
+    od = DeviceBuffer((t, n), local)
+    steps = max(args.steps, 5)
+    step_ms = np.zeros(steps)
+    kern_ms = np.zeros(steps)
+    launches = np.zeros(steps, dtype=np.int64)
+    _lib.call("gpb_benchmark_forward", prov.h, vd.cptr, od.cptr, t, args.warmup, steps, 0,
+              C.c_void_p(step_ms.ctypes.data), C.c_void_p(kern_ms.ctypes.data),
+              C.c_void_p(launches.ctypes.data))
+    mf_ms = float(np.median(step_ms))
+    dev = torch.device("cuda", local)
+    Xt = torch.from_numpy(X).to(dev) / torch.from_numpy(ell).to(dev)
+    Vt = torch.from_numpy(V).to(dev)
+    ev = [torch.cuda.Event(enable_timing=True) for _ in range(4)]
+
+    def fill():
+        sq = (Xt * Xt).sum(1)
+        K = sq[:, None] + sq[None, :] - 2.0 * (Xt @ Xt.T)
+        return torch.exp(-0.5 * K.clamp_min_(0.0))
+
+    K = fill()
+    torch.cuda.synchronize()
+    ev[0].record()
+    for _ in range(3):
+        K = fill()
+    ev[1].record()
+    torch.cuda.synchronize()
+    fill_ms = ev[0].elapsed_time(ev[1]) / 3
+    out = K @ Vt + 0.01 * Vt
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(steps):
+        ev[2].record()
+        out = K @ Vt
+        out.add_(Vt, alpha=0.01)
+        ev[3].record()
+        torch.cuda.synchronize()
+        times.append(ev[2].elapsed_time(ev[3]))
+    gemm_ms = float(np.median(times))
+    ref = od.download().T
+    err = float(np.linalg.norm(out.cpu().numpy() - ref) / np.linalg.norm(ref))
+    line = {
+        "metric": "K·V ms per product (matrix-free vs materialized)", "value": mf_ms, "unit": "ms",
+        "n_gpus": 1, "steps": steps, "warmup": args.warmup, "ms_per_step": mf_ms,
+        "higher_is_better": False, "scaling": "strong", "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (config 2 recipe inputs, RBF-ARD)",
+        "config": {"workload": "materialized-route comparison", "n": n, "d": d, "t": t,
+                   "tile_kernel": prov.matvec_layout(t)},
+        "materialized": {"fill_ms": fill_ms, "sgemm_ms": gemm_ms, "K_bytes": 4 * n * n,
+                         "sgemm_gbs": 4.0 * n * n / (gemm_ms * 1e-3) / 1e9,
+                         "products_to_amortise_fill": (fill_ms / (mf_ms - gemm_ms)
+                                                       if mf_ms > gemm_ms else None)},
+        "matrix_free_vs_sgemm_rel_diff": err,
+    }
+    print(json.dumps(line), flush=True)
+
+
 def run_config(args, rank: int, world: int, local: int) -> None:
     """Configs 1, 2 and 4 through the public model API on one GPU: a full fit
     (fit s/iter = median per-iteration time; the LMC fit, which records no
@@ -385,6 +465,9 @@ def main():
         return
     if args.workload == "c3fit":
         run_c3fit(args, rank, world, local)
+        return
+    if args.workload == "materialized":
+        run_materialized(args, rank, world, local)
         return
 
     from mojogp_b200 import _lib, synthetic

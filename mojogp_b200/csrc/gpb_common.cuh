@@ -108,6 +108,14 @@ __device__ __forceinline__ bool mbar_try_wait_hint(uint64_t* bar, uint32_t parit
   return ok != 0;
 }
 
+// Suspend-time hint (ns) for the polls of mbar_wait_bounded: a waiting thread
+// sleeps inside try_wait until the phase completes or the hint expires,
+// instead of re-issuing the poll (measured +1.4 % on the Gram K·V kernel,
+// whose 24 issuer and epilogue warps mostly wait); 0 = plain try_wait.
+#ifndef GPB_WAIT_HINT_NS
+#define GPB_WAIT_HINT_NS 20000
+#endif
+
 // Wait on an mbarrier phase for at most about `limit_ns`; returns false on
 // timeout. The clock is read once per 32 polls, so a spinning thread costs
 // few issue slots.
@@ -117,8 +125,11 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
   const uint64_t t0 = global_timer_ns();
   while (true) {
 #pragma unroll 1
-    for (int k = 0; k < 32; ++k)
-      if (mbar_try_wait(bar, parity)) return true;
+    for (int k = 0; k < 32; ++k) {
+      const bool done = GPB_WAIT_HINT_NS > 0 ? mbar_try_wait_hint(bar, parity, GPB_WAIT_HINT_NS)
+                                             : mbar_try_wait(bar, parity);
+      if (done) return true;
+    }
     if (global_timer_ns() - t0 > limit_ns) return false;
   }
 }

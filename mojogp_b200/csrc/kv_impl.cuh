@@ -70,8 +70,9 @@ int kv_launch_tc(const KvLaunch& L) {
 template <int DP, int LEAF>
 int kv_launch_gram(const KvLaunch& L) {
   auto kern = kv_tile_gram_kernel<DP, LEAF>;
-  const size_t smem = ((size_t)kGStages * gram_tile_floats(DP)) *
-                      sizeof(float);
+  constexpr int kThreads = kGThreads;
+  constexpr int kRows = kGEpiThreads;
+  const size_t smem = ((size_t)kGStages * gram_tile_floats(DP)) * sizeof(float);
   int dev = 0;
   GPB_CHECK_CUDA(cudaGetDevice(&dev));
   static int resident[64];
@@ -80,7 +81,7 @@ int kv_launch_gram(const KvLaunch& L) {
   if (dev < 0 || dev >= 64) dev = 0;
   if (!init[dev]) {
     GPB_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
-    GPB_CHECK_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&resident[dev], kern, kGThreads, smem));
+    GPB_CHECK_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&resident[dev], kern, kThreads, smem));
     GPB_CHECK_CUDA(cudaDeviceGetAttribute(&num_sms[dev], cudaDevAttrMultiProcessorCount, dev));
     if (resident[dev] < 1) resident[dev] = 1;
     // The kernel allocates all 512 TMEM columns: two CTAs must never share an SM.
@@ -88,7 +89,7 @@ int kv_launch_gram(const KvLaunch& L) {
                 resident[dev]);
     init[dev] = true;
   }
-  const int64_t row_blocks = ceil_div(L.nrow, kGEpiThreads);
+  const int64_t row_blocks = ceil_div(L.nrow, kRows);
   if (row_blocks == 0 || L.ntiles == 0) return GPB_OK;
   int splits = kv_choose_splits(row_blocks, L.ntiles, resident[dev], num_sms[dev]);
   if (splits > 1) {
@@ -105,7 +106,7 @@ int kv_launch_gram(const KvLaunch& L) {
     ep.out_ld = L.nrow;
   }
   if (L.ev_begin) GPB_CHECK_CUDA(cudaEventRecord(L.ev_begin, L.stream));
-  kern<<<dim3((unsigned)row_blocks, (unsigned)splits), kGThreads, smem, L.stream>>>(
+  kern<<<dim3((unsigned)row_blocks, (unsigned)splits), kThreads, smem, L.stream>>>(
       L.xrow, L.nrow, L.xv, L.ntiles, tiles_per_split, L.fp, ep, L.err);
   GPB_CHECK_CUDA(cudaGetLastError());
   if (L.launches) *L.launches += 1;
@@ -116,6 +117,7 @@ int kv_launch_gram(const KvLaunch& L) {
   if (L.ev_end) GPB_CHECK_CUDA(cudaEventRecord(L.ev_end, L.stream));
   return GPB_OK;
 }
+
 
 template <int DP, int LEAF, int NV>
 int kv_launch_gram1(const KvLaunch& L) {

@@ -145,3 +145,50 @@ def test_engine_predict_matches_model_predict(gpb_lib):
     assert again["alpha_cache_used"] and again["love_root_cache_used"]
     np.testing.assert_array_equal(again["mean"], out["mean"])
     np.testing.assert_array_equal(again["variance"], out["variance"])
+
+
+def test_alpha_cg_config5_recipe_cap(gpb_lib):
+    """The prediction-time alpha solve on the config-5 recipe (RBF-ARD, d = 8,
+    noise 0.01) at the reference's default settings (max 300 iterations,
+    relative residual 1e-3; solve_single_rhs_deterministic_host_jit,
+    jit_prediction.mojo:681-759: plain CG, no preconditioner). At n = 12000
+    the float64 restatement of that algorithm also stops at the 300 cap, so
+    a capped run at scale is the reference's behaviour, not this
+    implementation's; the float32 solve reaches a residual of the same order
+    (unconverged CG iterates themselves differ between float32 and float64)."""
+    from mojogp_b200 import synthetic
+    from oracle import kernels as ok
+    n = 12000
+    X, y, _, p, noise = synthetic.config5(n=n, n_test=1)
+    k = make_ard_kernel(RBF(ard=True), 8)
+    prov = Provider(X, k, p, noise)
+    yc = (y - y.mean()).astype(np.float32)
+    alpha, it = prediction.compute_alpha(prov, yc, 300, 1e-3)
+    A = ok.kernel_matrix(k.to_spec(8), p, X) + noise * np.eye(n)
+    b = yc.astype(np.float64)
+    ref, rit = ol.alpha_cg(A, b, 300, 1e-3)
+    assert rit == 300 and it == 300, (it, rit)
+    res_gpu = np.linalg.norm(b - A @ alpha) / np.linalg.norm(b)
+    res_ref = np.linalg.norm(b - A @ ref) / np.linalg.norm(b)
+    assert res_ref > 1e-3 and res_gpu < 3 * res_ref, (res_gpu, res_ref)
+
+
+def test_alpha_cg_config5_recipe_converged(gpb_lib):
+    """Same recipe with noise 0.1 (better conditioned): both solves converge
+    within the default budget and agree to the solve tolerance. float32 CG
+    needs more iterations than float64 here (112 against 88 on this B200: the
+    float32 residual recurrence loses orthogonality at condition ~1e4), so
+    the counts are held to within 1.5x, not equal."""
+    from mojogp_b200 import synthetic
+    from oracle import kernels as ok
+    n = 3000
+    X, y, _, p, _ = synthetic.config5(n=n, n_test=1)
+    noise = 0.1
+    k = make_ard_kernel(RBF(ard=True), 8)
+    prov = Provider(X, k, p, noise)
+    yc = (y - y.mean()).astype(np.float32)
+    alpha, it = prediction.compute_alpha(prov, yc, 300, 1e-3)
+    A = ok.kernel_matrix(k.to_spec(8), p, X) + noise * np.eye(n)
+    ref, rit = ol.alpha_cg(A, yc.astype(np.float64), 300, 1e-3)
+    assert it < 300 and rit < 300 and rit <= it <= 1.5 * rit, (it, rit)
+    assert np.linalg.norm(alpha - ref) / np.linalg.norm(ref) < 1e-2
