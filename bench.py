@@ -35,7 +35,14 @@ F_PER_PAIR_RBF = lambda d, t: 3 * d + 3 + 2 * t  # algorithmic flops per kernel 
 # DP = 16): MMA1 3xTF32 on x·y (3 * 2 * DP) + the norm k-step (2 * 8), MMA2
 # three tf32 products into t = 16 columns (3 * 2 * t).
 TC_PER_PAIR_GRAM = lambda dp, t: 3 * 2 * dp + 2 * 8 + 3 * 2 * t
+# fp16 Gram kernel (kind::f16, K = 16 per MMA): MMA1 is 4 k-steps of 16 at
+# DP = 16 (xh.bh, xl.bh, xh.bl, norms) or 2 at DP = 8, MMA2 one N = 32 and one
+# N = 16 product per column.
+TC_PER_PAIR_GRAMH = lambda dp, t: (4 if dp > 8 else 2) * 2 * 16 + 2 * 2 * t + 2 * t
 MUFU_PER_SM_CLK = 16  # MUFU (ex2) results per SM per clock on B200: 4 per sub-partition
+# DRAM bytes (read + write) of one fp16 Gram tile-kernel launch at n = 1e6, d = 16, t = 16 on one
+# GPU, from the one-pass ncu capture in profiles/kv_tile_gramh_rbf_ard_d16_t16.md.
+GRAMH_TRAFFIC_C3 = 784.76e6 + 196.19e6
 
 
 def parse():
@@ -554,18 +561,26 @@ def main():
     fp32_peak = {"achieved": achieved, "peak": peak_tf.value, "unit": "TFLOP/s",
                  "frac": achieved / peak_tf.value, "flops_per_pair": F,
                  "peak_source": "measured FFMA probe (gpb_measure_fp32_peak) on this GPU"}
-    if layout == "gram-tensor-core":
+    if layout in ("gram-tensor-core", "gram-tensor-core-tf32"):
+        f16 = layout == "gram-tensor-core"
         peaks_path = Path(__file__).resolve().parent / "MEASURED_PEAKS.json"
         try:
             bf16 = float(json.loads(peaks_path.read_text())["bf16_tflops"])
-            src = "of measured: MEASURED_PEAKS.json bf16_tflops (burst) / 2 = dense tf32"
+            src = "of measured: MEASURED_PEAKS.json bf16_tflops (burst)"
         except (OSError, KeyError, ValueError):
-            bf16, src = 1590.0, "of fallback: 1.59 PFLOP/s bf16 / 2 = dense tf32"
+            bf16, src = 1590.0, "of fallback: 1.59 PFLOP/s bf16"
+        peak = bf16 if f16 else bf16 / 2
+        src += " = dense f16" if f16 else " / 2 = dense tf32"
         dp = 16 if d > 8 else 8
-        tc = TC_PER_PAIR_GRAM(dp, 16)
+        tc = TC_PER_PAIR_GRAMH(dp, 16) if f16 else TC_PER_PAIR_GRAM(dp, 16)
         tc_achieved = pairs_per_s * tc / 1e12
-        roofline = {"bound": "tensor", "achieved": tc_achieved, "peak": bf16 / 2,
-                    "unit": "TFLOP/s", "frac": tc_achieved / (bf16 / 2), "traffic": None,
+        traffic = (GRAMH_TRAFFIC_C3 if f16 and world == 1 and (n, d, t) == (1_000_000, 16, 16)
+                   else None)
+        roofline = {"bound": "tensor", "achieved": tc_achieved, "peak": peak,
+                    "unit": "TFLOP/s", "frac": tc_achieved / peak, "traffic": traffic,
+                    "traffic_source": ("ncu dram__bytes_read.sum + dram__bytes_write.sum of one "
+                                       "launch at this size (profiles/kv_tile_gramh_rbf_ard_d16_t16.md)"
+                                       if traffic else "not captured for this configuration"),
                     "peak_source": src, "tensor_flops_per_pair": tc,
                     "mufu": {"achieved_per_sm_clk": pairs_per_s / 148 / (sm_mhz * 1e6),
                              "peak_per_sm_clk": MUFU_PER_SM_CLK,

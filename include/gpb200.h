@@ -395,9 +395,11 @@ int gpb_tc_selftest(int32_t device, int32_t variant, const float* a_host, const 
 
 /* Tile kernel the forward matvec uses for its first 16 columns (no reference
  * counterpart; diagnostics and tests): 0 scalar FFMA, 1 paired-row FFMA2,
- * 2 tensor-core contraction, 3 Gram form (both contractions on the tensor
- * core, chosen only for bounded prescaled input norms), 4 narrow Gram form
- * (tensor-core distances, fp32 CUDA-core contraction; 1-column chunks). */
+ * 2 tensor-core contraction, 3 Gram form on tf32 operands (both contractions
+ * on the tensor core, chosen only for bounded prescaled input norms, when
+ * GPB_KV_GRAMH=0), 4 narrow Gram form (tensor-core distances, fp32 CUDA-core
+ * contraction; 1-column chunks), 5 Gram form on fp16 operands (the default
+ * where 3 applies). */
 int gpb_matvec_layout(gpb_provider* p, int64_t ncols, int32_t* layout);
 
 /* Same result as gpb_forward_matvec, on the same tile kernel, but the call
@@ -407,11 +409,12 @@ int gpb_matvec_layout(gpb_provider* p, int64_t ncols, int32_t* layout);
  * memory pool or arena, or code where an allocation's implicit
  * synchronisation is not allowed). No counterpart in the reference.
  * Limit: 64 + S + round_up(n, 128) * W floats must fit in 8 Mi floats, where
- * W is the widest packed row over the call's 16-column chunks (72 on the Gram
- * layout at d <= 16, t = 16; 80 at d 17..32 when a 5..8-column chunk follows)
+ * W is the widest packed row over the call's 16-column chunks for either
+ * outcome of the Gram norm check (48 at d <= 16, t = 16; 80 at d 17..32 when
+ * a 5..8-column chunk follows)
  * and S = n * DP (DP = padded input dims) only when the provider's prescaled
  * inputs are stale (no product since the last parameter update). That is
- * about 116k rows at d = 16, t = 16 (95k when stale) and 104k rows at d = 32
+ * about 174k rows at d = 16, t = 16 (131k when stale) and 104k rows at d = 32
  * (75k when stale); larger n is rejected with GPB_ERR_INVALID. A stale call
  * reduces the input norms itself, with one stream synchronisation. The first
  * call on a device loads the array's module, so make that first call before

@@ -122,8 +122,23 @@ int Engine::matvec(float* v_local, int64_t v_ld, int t, float* out, int64_t out_
     const int W = kv_packed_width(p->eval, p->DP, T, p->gram_ok);
     GPB_TRY(xv.ensure((size_t)rows_total * W * sizeof(float)));
     float* mine = xv.f() + (int64_t)dist.rank * nl_pad * W;
-    GPB_TRY(k_pack(p->Xs_d + r0 * p->DP, p->DP, v_local, v_ld, c0, tcols, T, nl, nl_pad, mine,
-                   update_z, update_beta, st, layout));
+    if (layout == KV_GRAMH) {
+      // Column scales from the maxima over every rank's rows.
+      GPB_TRY(launch_gramh_colmax(v_local, v_ld, c0, tcols, nl, mine, update_z, update_beta,
+                                  p->DP, st));
+      if (world > 1) {
+        unsigned* mx = reinterpret_cast<unsigned*>(mine + gramh_max_offset(p->DP));
+        ncclResult_t r = ncclAllReduce(mx, mx, 16, ncclUint32, ncclMax, dist.comm, st);
+        GPB_REQUIRE(r == ncclSuccess, GPB_ERR_NCCL, "ncclAllReduce(max): %s",
+                    ncclGetErrorString(r));
+      }
+      GPB_TRY(launch_pack_gramh(p->Xs_d + r0 * p->DP, p->DP, v_local, v_ld, c0, tcols, nl, nl_pad,
+                                mine, update_z, update_beta, st, false));
+      p->launches += 1;
+    } else {
+      GPB_TRY(k_pack(p->Xs_d + r0 * p->DP, p->DP, v_local, v_ld, c0, tcols, T, nl, nl_pad, mine,
+                     update_z, update_beta, st, layout));
+    }
     p->launches += 1;
     if (world > 1) {
       ncclResult_t r = ncclAllGather(mine, xv.f(), (size_t)nl_pad * W, ncclFloat, dist.comm, st);

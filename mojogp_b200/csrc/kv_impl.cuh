@@ -118,6 +118,57 @@ int kv_launch_gram(const KvLaunch& L) {
   return GPB_OK;
 }
 
+template <int DP, int LEAF>
+int kv_launch_gramh(const KvLaunch& L) {
+  auto kern = kv_tile_gramh_kernel<DP, LEAF>;
+  constexpr int kThreads = kGHThreads;
+  constexpr int kRows = kGHEpiThreads;
+  const size_t smem = ((size_t)kGStages * gramh_tile_floats(DP)) * sizeof(float);
+  int dev = 0;
+  GPB_CHECK_CUDA(cudaGetDevice(&dev));
+  static int resident[64];
+  static bool init[64] = {false};
+  static int num_sms[64];
+  if (dev < 0 || dev >= 64) dev = 0;
+  if (!init[dev]) {
+    GPB_CHECK_CUDA(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem));
+    GPB_CHECK_CUDA(cudaOccupancyMaxActiveBlocksPerMultiprocessor(&resident[dev], kern, kThreads, smem));
+    GPB_CHECK_CUDA(cudaDeviceGetAttribute(&num_sms[dev], cudaDevAttrMultiProcessorCount, dev));
+    if (resident[dev] < 1) resident[dev] = 1;
+    // The kernel allocates all 512 TMEM columns: two CTAs must never share an SM.
+    GPB_REQUIRE(resident[dev] == 1, GPB_ERR_UNSUPPORTED, "Gram tile kernel: %d CTAs per SM",
+                resident[dev]);
+    init[dev] = true;
+  }
+  const int64_t row_blocks = ceil_div(L.nrow, kRows);
+  if (row_blocks == 0 || L.ntiles == 0) return GPB_OK;
+  int splits = kv_choose_splits(row_blocks, L.ntiles, resident[dev], num_sms[dev]);
+  if (splits > 1) {
+    const int64_t need_per_split = (int64_t)16 * L.nrow;
+    const int64_t cap = L.partial ? L.partial_capacity / need_per_split : 0;
+    if (cap < splits) splits = (int)(cap >= 2 ? cap : 1);
+  }
+  int tiles_per_split = (int)ceil_div(L.ntiles, splits);
+  splits = (int)ceil_div(L.ntiles, tiles_per_split);
+  TileEpilogue ep = L.ep;
+  ep.tcols = L.tcols;
+  if (splits > 1) {
+    ep.out = L.partial;
+    ep.out_ld = L.nrow;
+  }
+  if (L.ev_begin) GPB_CHECK_CUDA(cudaEventRecord(L.ev_begin, L.stream));
+  kern<<<dim3((unsigned)row_blocks, (unsigned)splits), kThreads, smem, L.stream>>>(
+      L.xrow, L.nrow, L.xv, L.ntiles, tiles_per_split, L.fp, ep, L.err);
+  GPB_CHECK_CUDA(cudaGetLastError());
+  if (L.launches) *L.launches += 1;
+  if (splits > 1) {
+    GPB_TRY(launch_kv_reduce(L, splits));
+    if (L.launches) *L.launches += 1;
+  }
+  if (L.ev_end) GPB_CHECK_CUDA(cudaEventRecord(L.ev_end, L.stream));
+  return GPB_OK;
+}
+
 
 template <int DP, int LEAF, int NV>
 int kv_launch_gram1(const KvLaunch& L) {
@@ -180,6 +231,7 @@ int kv_launch_one(const KvLaunch& L) {
   }
   if constexpr (!Ev::kGeneric && T == 16 && (DP == 8 || DP == 16)) {
     if constexpr (gram_leaf(Ev::kLeaf)) {
+      if (kv_layout(L.eval, DP, T, L.gram_ok) == KV_GRAMH) return kv_launch_gramh<DP, Ev::kLeaf>(L);
       if (kv_layout(L.eval, DP, T, L.gram_ok) == KV_GRAM) return kv_launch_gram<DP, Ev::kLeaf>(L);
     }
   }

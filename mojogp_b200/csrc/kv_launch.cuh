@@ -3,6 +3,7 @@
 #pragma once
 
 #include "kv_tiles.cuh"
+#include "kv_tiles_gramh.cuh"
 
 namespace gpb {
 
@@ -59,6 +60,9 @@ inline int kv_pick_t(int64_t remaining) {
 }
 
 // Kernel / packed-layout choice per launch shape:
+//   KV_GRAMH  the Gram form on fp16 hi / lo operands (kv_tiles_gramh.cuh):
+//             the default for every KV_GRAM case; GPB_KV_GRAMH=0 in the
+//             environment selects KV_GRAM instead;
 //   KV_GRAM   both contractions on the tensor core (kv_tiles_gram.cuh): RBF,
 //             Matérn-3/2, Matérn-5/2 or RQ, T = 16, DP 8 or 16, and only when
 //             the caller vouches for bounded input norms (gram_ok);
@@ -75,11 +79,12 @@ inline int kv_pick_t(int64_t remaining) {
 //   KV_X2     paired-row FFMA2 kernel (kv_tiles_x2.cuh): fast leaves, even DP,
 //             T >= 4; GPB_KV_SCALAR=1 disables it (and the TC kernel);
 //   KV_SCALAR everything else (and the composite-tree evaluator).
-enum KvLayout { KV_SCALAR = 0, KV_X2 = 1, KV_TC = 2, KV_GRAM = 3, KV_GRAM1 = 4 };
+enum KvLayout { KV_SCALAR = 0, KV_X2 = 1, KV_TC = 2, KV_GRAM = 3, KV_GRAM1 = 4, KV_GRAMH = 5 };
 bool kv_x2_disabled();
 bool kv_tc_disabled();
 bool kv_gram_disabled();
 bool kv_gram1_disabled();
+bool kv_gramh_disabled();
 // Largest max_i |x'_i|^2 (prescaled inputs) for which the Gram expansion keeps
 // the matvec within the 1e-5 relative bar (3xTF32 cross term, fp32 norms).
 constexpr float kGramMaxSqNorm = 100.f;
@@ -91,7 +96,7 @@ inline int kv_layout(int eval, int DP, int T, bool gram_ok = false) {
   if (eval == kEvalGeneric || kv_x2_disabled()) return KV_SCALAR;
   if (gram_ok && gram_leaf(eval) && (DP == 8 || DP == 16) && !kv_tc_disabled() &&
       !kv_gram_disabled()) {
-    if (T == 16) return KV_GRAM;
+    if (T == 16) return kv_gramh_disabled() ? KV_GRAM : KV_GRAMH;
     if (T == 1 && !kv_gram1_disabled()) return KV_GRAM1;
   }
   if (T == 16 && DP % 4 == 0 && DP <= 32 && !kv_tc_disabled()) return KV_TC;
@@ -105,7 +110,7 @@ inline int kv_layout(int eval, int DP, int T, bool gram_ok = false) {
 inline int kv_chunk_t(int eval, int DP, int64_t remaining, bool gram_ok) {
   const int t = kv_pick_t(remaining);
   if (t < 16 && kv_layout(eval, DP, t, gram_ok) != KV_GRAM1 &&
-      kv_layout(eval, DP, 16, gram_ok) == KV_GRAM)
+      (kv_layout(eval, DP, 16, gram_ok) == KV_GRAM || kv_layout(eval, DP, 16, gram_ok) == KV_GRAMH))
     return 16;
   return t;
 }
@@ -115,6 +120,7 @@ inline bool kv_uses_x2(int eval, int DP, int T) { return kv_layout(eval, DP, T) 
 inline int kv_packed_width(int eval, int DP, int T, bool gram_ok = false) {
   switch (kv_layout(eval, DP, T, gram_ok)) {
     case KV_GRAM: return 2 * DP + 8 + 32;
+    case KV_GRAMH: return gramh_tile_floats(DP) / 128;
     case KV_GRAM1: return 2 * DP + 8 + T;
     case KV_TC: return DP + 32;
     case KV_X2: return 2 * (DP + T);

@@ -4,6 +4,7 @@
 #include "matvec.cuh"
 #include "kv_tiles_tc.cuh"
 #include "kv_tiles_gram.cuh"
+#include "kv_tiles_gramh.cuh"
 
 #include <cstdlib>
 
@@ -288,6 +289,141 @@ int launch_pack_gram(const float* xs, int DP, float* v, int64_t v_ld, int c0, in
   return GPB_OK;
 }
 
+// ---------------------------------------------------------- fp16 Gram tiles
+// Column value of the packed right-hand side, with the optional in-place
+// p = z + beta p update of the CG direction (not written back here).
+__device__ __forceinline__ float gramh_col_value(const float* v, int64_t v_ld, int c0, int c,
+                                                 int64_t j, const float* upd_z,
+                                                 const float* upd_beta) {
+  const int64_t off = (int64_t)(c0 + c) * v_ld + j;
+  float val = v[off];
+  if (upd_beta) {
+    const float b = upd_beta[c0 + c];
+    const float zz = upd_z[off];
+    val = (b == 0.f || b != b || val != val) ? zz : fmaf(b, val, zz);
+  }
+  return val;
+}
+
+// maxbits[c] = max over rows j < n of |column c| (float bit patterns; the
+// caller zeroes them). NaN maps above every finite value.
+__global__ void gramh_colmax_kernel(const float* __restrict__ v, int64_t v_ld, int c0, int tcols,
+                                    int64_t n, const float* __restrict__ upd_z,
+                                    const float* __restrict__ upd_beta,
+                                    unsigned* __restrict__ maxbits) {
+  float m[16];
+#pragma unroll
+  for (int c = 0; c < 16; ++c) m[c] = 0.f;
+  for (int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; j < n;
+       j += (int64_t)gridDim.x * blockDim.x) {
+#pragma unroll
+    for (int c = 0; c < 16; ++c) {
+      if (c >= tcols) break;
+      const float a = fabsf(gramh_col_value(v, v_ld, c0, c, j, upd_z, upd_beta));
+      m[c] = (a != a) ? a : fmaxf(m[c], a);
+    }
+  }
+#pragma unroll
+  for (int c = 0; c < 16; ++c) {
+    if (c >= tcols) break;
+    unsigned b = __float_as_uint(m[c]);
+    if (m[c] != m[c]) b = 0x7FC00000u;
+    for (int o = 16; o > 0; o >>= 1) b = max(b, __shfl_xor_sync(0xffffffffu, b, o));
+    if ((threadIdx.x & 31) == 0 && b) atomicMax(&maxbits[c], b);
+  }
+}
+
+// One packed fp16 Gram tile row per column j (see kv_tiles_gramh.cuh).
+__global__ void pack_gramh_kernel(const float* __restrict__ xs, int DP, float* __restrict__ v,
+                                  int64_t v_ld, int c0, int tcols, int64_t n, int64_t npad,
+                                  float* __restrict__ dst, const float* __restrict__ upd_z,
+                                  const float* __restrict__ upd_beta,
+                                  const unsigned* __restrict__ maxbits) {
+  const int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+  if (j >= npad) return;
+  const int TILE = DP == 16 ? gramh_tile_floats(16) : gramh_tile_floats(8);
+  float* base = dst + (j / 128) * TILE;
+  const int jt = (int)(j % 128);
+  __half* hb = reinterpret_cast<__half*>(base);
+  float y[16];
+  for (int q = 0; q < DP; ++q) y[q] = (j < n) ? kGHInScale * xs[j * DP + q] : 0.f;
+  float m3[3];
+  gramh_split3(gram_sqnorm(y, DP), m3[0], m3[1], m3[2]);
+  const float ny[8] = {1.f, 1.f, 1.f, m3[0], m3[1], m3[2], 0.f, 0.f};
+  auto put = [&](int blk, int k, float val) {
+    hb[blk * 2048 + gramh_boff(jt, k, 2048) / 2] = __float2half_rn(val);
+  };
+  for (int q = 0; q < DP; ++q) {
+    const float b = -2.f * y[q];
+    const float bh = __half2float(__float2half_rn(b));
+    const float bl = b - bh;
+    if (DP == 16) {
+      put(0, q, bh);
+      put(1, q, bl);
+    } else {
+      put(0, q, bh);
+      put(0, 8 + q, bh);
+      put(1, q, bl);
+    }
+  }
+  if (DP == 16) {
+    for (int k = 0; k < 16; ++k) put(2, k, k < 8 ? ny[k] : 0.f);
+  } else {
+    for (int k = 0; k < 8; ++k) put(1, 8 + k, ny[k]);
+  }
+  // V block of chunk jt / 16: rows [V hi (16) | V lo (16)], k = jt % 16.
+  __half* vb = hb + 2 * gramh_v_offset(DP) + (jt / 16) * 512;
+  const int k = jt % 16;
+  for (int c = 0; c < 16; ++c) {
+    float val = 0.f;
+    if (j < n && c < tcols) {
+      val = gramh_col_value(v, v_ld, c0, c, j, upd_z, upd_beta);
+      if (upd_beta) v[(int64_t)(c0 + c) * v_ld + j] = val;
+    }
+    const float sv = val * gramh_col_scale(__uint_as_float(maxbits[c]));
+    const __half h = __float2half_rn(sv);
+    vb[gramh_boff(c, k, 512) / 2] = h;
+    vb[gramh_boff(16 + c, k, 512) / 2] = __float2half_rn(sv - __half2float(h));
+  }
+  base[gramh_max_offset(DP) + jt] = jt < 16 ? __uint_as_float(maxbits[jt]) : 0.f;
+}
+
+int launch_gramh_colmax(float* v, int64_t v_ld, int c0, int tcols, int64_t n, float* dst,
+                        const float* upd_z, const float* upd_beta, int DP, cudaStream_t stream) {
+  unsigned* maxbits = reinterpret_cast<unsigned*>(dst + gramh_max_offset(DP));
+  GPB_CHECK_CUDA(cudaMemsetAsync(maxbits, 0, 16 * sizeof(unsigned), stream));
+  if (n <= 0) return GPB_OK;
+  const unsigned blocks = (unsigned)std::min<int64_t>(ceil_div(n, 256), 4 * 148);
+  gramh_colmax_kernel<<<blocks, 256, 0, stream>>>(v, v_ld, c0, tcols, n, upd_z, upd_beta, maxbits);
+  GPB_CHECK_CUDA(cudaGetLastError());
+  return GPB_OK;
+}
+
+int launch_pack_gramh(const float* xs, int DP, float* v, int64_t v_ld, int c0, int tcols,
+                      int64_t n, int64_t npad, float* xv, const float* upd_z,
+                      const float* upd_beta, cudaStream_t stream, bool colmax) {
+  if (npad == 0) return GPB_OK;
+  GPB_REQUIRE(DP == 8 || DP == 16, GPB_ERR_INVALID, "fp16 Gram packing needs DP in {8,16}");
+  if (colmax)
+    GPB_TRY(launch_gramh_colmax(v, v_ld, c0, tcols, n, xv, upd_z, upd_beta, DP, stream));
+  // Every block reads the maxima from tile 0's tail; block 0 rewrites the same
+  // values there.
+  const unsigned* maxbits = reinterpret_cast<const unsigned*>(xv + gramh_max_offset(DP));
+  pack_gramh_kernel<<<(unsigned)ceil_div(npad, 128), 128, 0, stream>>>(
+      xs, DP, v, v_ld, c0, tcols, n, npad, xv, upd_z, upd_beta, maxbits);
+  GPB_CHECK_CUDA(cudaGetLastError());
+  return GPB_OK;
+}
+
+bool kv_gramh_disabled() {
+  static int v = -1;
+  if (v < 0) {
+    const char* e = getenv("GPB_KV_GRAMH");
+    v = (e && e[0] == '0') ? 1 : 0;
+  }
+  return v == 1;
+}
+
 bool kv_gram1_disabled() {
   static int v = -1;
   if (v < 0) {
@@ -328,6 +464,9 @@ int launch_pack(const float* xs, int DP, const float* v, int64_t v_ld, int tcols
   if (layout == KV_GRAM1)
     return launch_pack_gram1(xs, DP, T, const_cast<float*>(v), v_ld, 0, tcols, n, npad, xv,
                              nullptr, nullptr, stream);
+  if (layout == KV_GRAMH)
+    return launch_pack_gramh(xs, DP, const_cast<float*>(v), v_ld, 0, tcols, n, npad, xv, nullptr,
+                             nullptr, stream, true);
   if (layout == KV_X2) {
     pack_dup_kernel<<<(unsigned)ceil_div(npad, 256), 256, 0, stream>>>(xs, DP, v, v_ld, tcols, T,
                                                                       n, npad, xv);

@@ -32,4 +32,14 @@ int launch_pack_gram1(const float* xs, int DP, int NV, float* v, int64_t v_ld, i
                       int64_t n, int64_t npad, float* xv, const float* upd_z,
                       const float* upd_beta, cudaStream_t stream);
 
+// fp16 Gram tile packing (KV_GRAMH), same arguments. With `colmax` the
+// column maxima are first reduced into tile 0's tail; without it the caller
+// has put them there (the sharded engine all-reduces them between the two).
+int launch_pack_gramh(const float* xs, int DP, float* v, int64_t v_ld, int c0, int tcols,
+                      int64_t n, int64_t npad, float* xv, const float* upd_z,
+                      const float* upd_beta, cudaStream_t stream, bool colmax);
+// Zeroes dst's tile-0 column-maximum slots and reduces max |v_c| into them.
+int launch_gramh_colmax(float* v, int64_t v_ld, int c0, int tcols, int64_t n, float* dst,
+                        const float* upd_z, const float* upd_beta, int DP, cudaStream_t stream);
+
 }  // namespace gpb

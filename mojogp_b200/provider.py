@@ -158,7 +158,8 @@ class Provider:
     def forward_matvec(self, out: DeviceBuffer, v: DeviceBuffer, ncols: int) -> None:
         _lib.call("gpb_forward_matvec", self.h, out.cptr, v.cptr, int(ncols))
 
-    LAYOUTS = {0: "scalar", 1: "ffma2", 2: "tensor-core", 3: "gram-tensor-core", 4: "gram-narrow"}
+    LAYOUTS = {0: "scalar", 1: "ffma2", 2: "tensor-core", 3: "gram-tensor-core-tf32", 4: "gram-narrow",
+               5: "gram-tensor-core"}
 
     def matvec_layout(self, ncols: int = 16) -> str:
         """Name of the tile kernel the forward matvec uses for `ncols` columns."""

@@ -74,7 +74,9 @@ def test_two_gpu_sharded_engine_matches_one_gpu(gpb_lib, tmp_path):
     # Pivot list of the sharded argmax: identical to one GPU.
     assert two["pivots"] == one["pivots"]
     # Config-3 recipe sharded product: every rank's row sample within the
-    # 1e-5 matvec bar of the float64 oracle, and the fixed rows equal to one GPU.
+    # 1e-5 matvec bar of the float64 oracle, and the fixed rows equal to one GPU
+    # to that bar (the shards split the column range differently, so the
+    # summation orders differ).
     for part in one["c3"] + two["c3"]:
         assert part["c3_layout"] == "gram-tensor-core"
         assert part["c3_err"] < 1e-5, part["c3_err"]
@@ -83,4 +85,4 @@ def test_two_gpu_sharded_engine_matches_one_gpu(gpb_lib, tmp_path):
     a, b = rows(one["c3"]), rows(two["c3"])
     assert sorted(a) == sorted(b)
     for r in a:
-        np.testing.assert_allclose(b[r], a[r], rtol=1e-6, atol=1e-6)
+        np.testing.assert_allclose(b[r], a[r], rtol=1e-5, atol=1e-5)
