@@ -13,9 +13,12 @@
 //             (2 MMAs, was 6); D[:, 0:16] + D[:, 16:32] is the product.
 // An fp16 hi / lo pair carries 22 significant bits, as a tf32 pair does. The
 // range is handled by exact power-of-two scalings:
-//   * inputs: x'' = 16 x', so u'' = 256 u (|x'|^2 <= 100 by the Gram gate:
-//     every operand stays inside fp16's normal range except components below
-//     2^-7, whose lo parts lose bits far below the 1e-5 bar);
+//   * inputs: the row side carries x'' = 16 x', the column side -2 y' / 16
+//     (so the cross term is -2 x'.y' unscaled); |x'|^2 <= 100 by the Gram
+//     gate keeps every operand inside fp16's normal range except components
+//     below 2^-7, whose lo parts lose bits far below the 1e-5 bar. The norm
+//     k-step also adds -12, so MMA1 yields u - 12 and the RBF value
+//     k * 2^12 = 2^-(u - 12) is one MUFU ex2;
 //   * kernel values: the lo part of k * 2^12 stays normal down to k ~ 2^-14;
 //   * right-hand sides: column c is scaled by 2^e_c so that its largest
 //     magnitude lies in [2^12, 2^13) (colmax pass before packing; the raw
@@ -34,7 +37,9 @@
 // stages per row tile. Measured on this B200 at config 3: 202 TF/s with chunk
 // pairs against 175 with one chunk per pass (the epilogue is bound by its
 // TMEM load / store round trips) and 190 with 2 row tiles and two epilogue
-// warpgroups per row tile (fewer issuers and rows per CTA).
+// warpgroups per row tile (fewer issuers and rows per CTA); three MMA1 issuer
+// warps per row tile instead of two measured 185 (more threads, fewer
+// registers per thread).
 // TMEM: accumulators [0, 192) (32 per row tile and class), row operands
 // [192, 264) (three 8-column fp16 segments per row tile), stages
 // [272, 512) (16 per stage: u in fp32, then K hi | K lo as fp16 pairs).
@@ -60,8 +65,8 @@ constexpr uint32_t kGHColS = 272;    // + 80 r + 16 st
 static_assert(kGHColAcc + 32 * kGHPar * kGHRowTiles <= kGHColA, "TMEM map");
 static_assert(kGHColA + 24 * kGHRowTiles <= kGHColS, "TMEM map");
 static_assert(kGHColS + 16 * kGHUStages * kGHRowTiles <= 512, "TMEM budget");
-constexpr float kGHInScale = 16.f;        // x'' = 16 x'
-constexpr float kGHUInv = 1.f / 256.f;    // u = u'' / 256
+constexpr float kGHInScale = 16.f;        // row side x'' = 16 x'; column side -2 y' / 16
+constexpr float kGHUShift = 12.f;         // MMA1 yields u - 12, so 2^-(u - 12) = k * 2^12
 constexpr float kGHKScale = 4096.f;       // K is carried as k * 2^12
 
 __host__ __device__ constexpr int gramh_blocks(int DP) { return DP == 16 ? 3 : 2; }
@@ -180,7 +185,9 @@ __global__ void __launch_bounds__(kGHThreads, 1) kv_tile_gramh_kernel(
     float x[DP];
 #pragma unroll
     for (int k = 0; k < DP; ++k) x[k] = i < nrow ? kGHInScale * xrow[i * DP + k] : 0.f;
-    float e[8] = {0.f, 0.f, 0.f, 1.f, 1.f, 1.f, 0.f, 0.f};
+    // [|x''|^2 parts | 1 1 1 | 1 (times -12) | 0]; the column side carries
+    // 2^-8 on the first three slots, |y'|^2 on the next three, -12 on the 7th.
+    float e[8] = {0.f, 0.f, 0.f, 1.f, 1.f, 1.f, 1.f, 0.f};
     gramh_split3(gram_sqnorm(x, DP), e[0], e[1], e[2]);
     const uint32_t a_row = tmem + lane_off + kGHColA + rt * 24;
     uint32_t hi[8], lo[8];
@@ -320,11 +327,11 @@ __global__ void __launch_bounds__(kGHThreads, 1) kv_tile_gramh_kernel(
         const float u0 = __uint_as_float(ub[h]), u1 = __uint_as_float(ub[h + 1]);
         float k0, k1;
         if constexpr (LEAF == GPB_KERNEL_RBF) {
-          k0 = ex2_approx(fmaf(u0, -kGHUInv, 12.f));
-          k1 = ex2_approx(fmaf(u1, -kGHUInv, 12.f));
+          k0 = ex2_approx(-u0);
+          k1 = ex2_approx(-u1);
         } else {
-          k0 = kGHKScale * FastEval<LEAF>::value(u0 * kGHUInv, fp);
-          k1 = kGHKScale * FastEval<LEAF>::value(u1 * kGHUInv, fp);
+          k0 = kGHKScale * FastEval<LEAF>::value(u0 + kGHUShift, fp);
+          k1 = kGHKScale * FastEval<LEAF>::value(u1 + kGHUShift, fp);
         }
         split_h2(k0, k1, hi[h / 2], lo[h / 2]);
       }

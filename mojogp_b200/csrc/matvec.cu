@@ -347,14 +347,18 @@ __global__ void pack_gramh_kernel(const float* __restrict__ xs, int DP, float* _
   __half* hb = reinterpret_cast<__half*>(base);
   float y[16];
   for (int q = 0; q < DP; ++q) y[q] = (j < n) ? kGHInScale * xs[j * DP + q] : 0.f;
+  // Norm row of the column side: 2^-8 against the row's |x''|^2 parts, |y'|^2
+  // = |y''|^2 / 256 in three parts against the row's ones, -12 against its
+  // last one (MMA1 then yields u - 12).
   float m3[3];
-  gramh_split3(gram_sqnorm(y, DP), m3[0], m3[1], m3[2]);
-  const float ny[8] = {1.f, 1.f, 1.f, m3[0], m3[1], m3[2], 0.f, 0.f};
+  gramh_split3(gram_sqnorm(y, DP) * (1.f / 256.f), m3[0], m3[1], m3[2]);
+  const float c8 = 1.f / 256.f;
+  const float ny[8] = {c8, c8, c8, m3[0], m3[1], m3[2], -kGHUShift, 0.f};
   auto put = [&](int blk, int k, float val) {
     hb[blk * 2048 + gramh_boff(jt, k, 2048) / 2] = __float2half_rn(val);
   };
   for (int q = 0; q < DP; ++q) {
-    const float b = -2.f * y[q];
+    const float b = y[q] * (-2.f / 256.f);  // -2 y'' / 256 = -2 y' / 16
     const float bh = __half2float(__float2half_rn(b));
     const float bl = b - bh;
     if (DP == 16) {
