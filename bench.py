@@ -8,8 +8,9 @@ n/N rows of the output; X and V are replicated) and every step ends with the
 NCCL all-gather of the output row blocks, as one CG iteration needs.
 
 Prints one JSON line (rank 0). `--impl reference` times the reference's CPU
-route (NumPy kernel evaluator + BLAS, restated in oracle/cpu_baseline.py) on
-the host cores instead.
+route on the host cores instead: its own NumPy kernel evaluator
+(KernelNode.evaluate, installed unmodified under baseline/_ref) + BLAS, or the
+restatement in oracle/cpu_baseline.py where that install is absent.
 """
 from __future__ import annotations
 
@@ -151,19 +152,61 @@ def run_fit(X, y, iters: int, local: int, comm) -> dict:
                         "tile_kernels": kinds}}
 
 
+def reference_matvec_sample(X, V, ell, target_s: float, max_rows: int, threads: int):
+    """Time the reference's own CPU route where it is installed (baseline/_ref):
+    its NumPy kernel evaluator KernelNode.evaluate (mojogp/kernel.py:722-923)
+    on row blocks x all columns, then a BLAS product with V, row blocks spread
+    over host threads. Returns (result dict, kind), kind "reference"; falls
+    back to the restatement in oracle/cpu_baseline.py (kind "port") when the
+    reference package does not import."""
+    import concurrent.futures as cf
+    ref_dir = ROOT / "baseline" / "_ref"
+    try:
+        if str(ref_dir) not in sys.path:
+            sys.path.insert(0, str(ref_dir))
+        from mojogp.kernel import RBF as RefRBF, make_ard_kernel as ref_ard
+    except Exception:  # the reference is not installed here: use the restatement
+        from oracle import cpu_baseline
+        return cpu_baseline.time_matvec_sample(X, V, ell, 1.0, target_s=target_s, threads=threads,
+                                               max_rows=max_rows), "port"
+    d = X.shape[1]
+    kern = ref_ard(RefRBF(ard=True), d)
+    params = np.concatenate([np.asarray(ell, np.float64), [1.0]])
+    V64 = V.astype(np.float64)
+    n = X.shape[0]
+
+    def rows_block(r0, r1):
+        K = kern.evaluate(X[r0:r1], X, params=params)
+        return np.asarray(K, np.float64) @ V64
+
+    def run(nrows, blk=16):  # 16 rows x n columns of float64 temporaries per thread
+        t0 = time.perf_counter()
+        with cf.ThreadPoolExecutor(threads) as ex:
+            list(ex.map(lambda r: rows_block(r, min(r + blk, nrows)), range(0, nrows, blk)))
+        return time.perf_counter() - t0
+
+    dt = run(min(64, n))
+    nrows = int(min(max_rows, n, max(64, 64 * target_s / max(dt, 1e-3))))
+    nrows = max(64, nrows // 64 * 64)
+    dt = run(nrows)
+    return {"seconds": dt, "rows": nrows, "pairs": nrows * n, "pairs_per_s": nrows * n / dt,
+            "threads": threads}, "reference"
+
+
 def run_reference(args, rank: int, world: int) -> None:
     """CPU arm: the reference's NumPy route on the host cores (rank 0 only)."""
     if rank != 0:
         return
     from mojogp_b200 import synthetic
-    from oracle import cpu_baseline
     X, _, ell = synthetic.config3(n=args.n, d=args.d)
     V = synthetic.probes_v(args.n, args.t, seed=1)
     threads = os.cpu_count() or 1
     per_step = []
+    kind = "port"
     for it in range(args.warmup + args.steps):
-        r = cpu_baseline.time_matvec_sample(X, V, ell, 1.0, target_s=max(2.0, 30.0 / max(args.steps + args.warmup, 1)),
-                                            threads=threads, max_rows=2048)
+        r, kind = reference_matvec_sample(
+            X, V, ell, target_s=max(2.0, 30.0 / max(args.steps + args.warmup, 1)),
+            max_rows=2048, threads=threads)
         if it >= args.warmup:
             per_step.append(r)
     F = F_PER_PAIR_RBF(args.d, args.t)
@@ -178,9 +221,11 @@ def run_reference(args, rank: int, world: int) -> None:
         "data": "synthetic (config 3 recipe, seed 3)",
         "config": {"workload": "config3 K(X,X)V RBF-ARD", "n": args.n, "d": args.d, "t": args.t,
                    "sample": f"{rows} rows x {args.n} columns per step"},
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": "port",
-                         "sample": f"{rows} output rows x all {args.n} columns, float64 NumPy "
-                                   "evaluator (kernel.py:804-923 route) + BLAS"},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": threads, "kind": kind,
+                         "sample": f"{rows} output rows x all {args.n} columns: "
+                                   + ("the reference's KernelNode.evaluate (baseline/_ref) + BLAS"
+                                      if kind == "reference" else
+                                      "float64 NumPy evaluator restated (kernel.py:804-923) + BLAS")},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -605,14 +650,15 @@ def main():
         "fit": fit,
     }
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        from oracle import cpu_baseline
-        Xs = X
-        r = cpu_baseline.time_matvec_sample(Xs, V, ell, 1.0, target_s=args.cpu_seconds,
-                                            max_rows=1024)
+        r, kind = reference_matvec_sample(X, V, ell, target_s=args.cpu_seconds, max_rows=1024,
+                                          threads=os.cpu_count() or 1)
         line["cpu_baseline"] = {
             "value": r["pairs_per_s"] * F / 1e12, "unit": UNIT, "cores": r["threads"],
-            "kind": "port",
-            "sample": f"{r['rows']} output rows x all {n} columns (float64 NumPy evaluator + BLAS)"}
+            "kind": kind,
+            "sample": f"{r['rows']} output rows x all {n} columns: "
+                      + ("the reference's KernelNode.evaluate (baseline/_ref) + BLAS"
+                         if kind == "reference" else
+                         "float64 NumPy evaluator restated (kernel.py:804-923) + BLAS")}
     if rank == 0:
         print(json.dumps(line), flush=True)
     if comm:
