@@ -643,6 +643,10 @@ def main():
                    "t": t, "parallelism": f"row-shard x{world}", "tile_kernel": layout,
                    "l2": "256 MB flush before every step; packed column tiles 128 MB"},
         "gpu_launches": int(launches.sum()),
+        "step_split_ms": {"tile_kernel": kmean, "pack_and_exchange": total_ms / steps - kmean,
+                          "note": "mean over the timed steps, max over ranks; pack_and_exchange "
+                                  "= packing, the colmax all-reduce and the NCCL all-gather of "
+                                  "the packed column tiles (0 exchange on 1 GPU)"},
         "e2e": {"value": e2e_tf, "unit": UNIT, "h2d_bytes_per_step": int(Vc.nbytes),
                 "d2h_bytes_per_step": int(Vc.nbytes)},
         "roofline": roofline,

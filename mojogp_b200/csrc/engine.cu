@@ -172,6 +172,8 @@ int Engine::matvec(float* v_local, int64_t v_ld, int t, float* out, int64_t out_
     L.stream = st;
     L.launches = &p->launches;
     L.gram_ok = p->gram_ok;
+    if (c0 == 0) L.ev_begin = p->tile_ev[0];
+    if (c0 + 16 >= t) L.ev_end = p->tile_ev[1];
     GPB_TRY(launch_kv(L));
   }
   return GPB_OK;
