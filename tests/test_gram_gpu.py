@@ -142,3 +142,22 @@ def test_gram_gradient_bilinear_vs_oracle(gpb_lib, kname, n, d, t):
     rd, rt = ok.gradient_bilinear(k.to_spec(d), p, X, A, B)
     np.testing.assert_allclose(data, rd, rtol=1e-4, atol=1e-4 * np.abs(rd).max())
     np.testing.assert_allclose(trace, rt, rtol=1e-4, atol=1e-4 * np.abs(rt).max())
+
+
+def test_gram_fp16_column_scaling(gpb_lib):
+    """The fp16 Gram path scales every right-hand-side column by a power of two
+    from its own maximum: columns of very different magnitudes (and an all-zero
+    column) in one product each meet the 1e-5 bar on their own."""
+    k, p, X, _ = _setup("rbf_ard", 2500, 16, 16, seed=77)
+    prov = Provider(X, k, p, 0.1)
+    assert prov.matvec_layout(16) == "gram-tensor-core"
+    rng = np.random.default_rng(78)
+    mags = [1e-8, 1e-3, 1.0, 1e4, 1e8, 0.0, 3.0, 1e-20, 1e20, 1.0, 2.0, 5e-5, 7e6, 1.0, 1.0, 1.0]
+    V = (rng.standard_normal((2500, 16)) * np.asarray(mags)[None, :]).astype(np.float32)
+    got = prov.matvec_host(V)
+    ref = ok.forward_matvec(k.to_spec(16), p, X, V, noise=0.1)
+    for c, m in enumerate(mags):
+        if m == 0.0:
+            assert np.all(got[:, c] == 0.0)
+        else:
+            assert rel_fro(got[:, c], ref[:, c]) < 1e-5, (c, m)
