@@ -397,9 +397,9 @@ int gpb_tc_selftest(int32_t device, int32_t variant, const float* a_host, const 
  * counterpart; diagnostics and tests): 0 scalar FFMA, 1 paired-row FFMA2,
  * 2 tensor-core contraction, 3 Gram form on tf32 operands (both contractions
  * on the tensor core, chosen only for bounded prescaled input norms, when
- * GPB_KV_GRAMH=0), 4 narrow Gram form (tensor-core distances, fp32 CUDA-core
+ * GPB_KV_GRAMH=0, and by default for the Matern and RQ leaves), 4 narrow Gram form (tensor-core distances, fp32 CUDA-core
  * contraction; 1-column chunks), 5 Gram form on fp16 operands (the default
- * where 3 applies). */
+ * for RBF where 3 applies; every Gram leaf with GPB_KV_GRAMH=2). */
 int gpb_matvec_layout(gpb_provider* p, int64_t ncols, int32_t* layout);
 
 /* Same result as gpb_forward_matvec, on the same tile kernel, but the call

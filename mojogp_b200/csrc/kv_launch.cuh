@@ -61,8 +61,10 @@ inline int kv_pick_t(int64_t remaining) {
 
 // Kernel / packed-layout choice per launch shape:
 //   KV_GRAMH  the Gram form on fp16 hi / lo operands (kv_tiles_gramh.cuh):
-//             the default for every KV_GRAM case; GPB_KV_GRAMH=0 in the
-//             environment selects KV_GRAM instead;
+//             the default for RBF (measured 4-12 % faster than KV_GRAM), while
+//             the Matern and RQ leaves keep KV_GRAM (their longer leaf
+//             evaluation made the fp16 kernel 0-11 % slower);
+//             GPB_KV_GRAMH=0 disables it, =2 takes it for every Gram leaf;
 //   KV_GRAM   both contractions on the tensor core (kv_tiles_gram.cuh): RBF,
 //             Matérn-3/2, Matérn-5/2 or RQ, T = 16, DP 8 or 16, and only when
 //             the caller vouches for bounded input norms (gram_ok);
@@ -84,7 +86,9 @@ bool kv_x2_disabled();
 bool kv_tc_disabled();
 bool kv_gram_disabled();
 bool kv_gram1_disabled();
-bool kv_gramh_disabled();
+// fp16 Gram kernel selection (GPB_KV_GRAMH): 0 never, 1 RBF only (default),
+// 2 every Gram leaf.
+int kv_gramh_mode();
 // Largest max_i |x'_i|^2 (prescaled inputs) for which the Gram expansion keeps
 // the matvec within the 1e-5 relative bar (3xTF32 cross term, fp32 norms).
 constexpr float kGramMaxSqNorm = 100.f;
@@ -96,7 +100,10 @@ inline int kv_layout(int eval, int DP, int T, bool gram_ok = false) {
   if (eval == kEvalGeneric || kv_x2_disabled()) return KV_SCALAR;
   if (gram_ok && gram_leaf(eval) && (DP == 8 || DP == 16) && !kv_tc_disabled() &&
       !kv_gram_disabled()) {
-    if (T == 16) return kv_gramh_disabled() ? KV_GRAM : KV_GRAMH;
+    if (T == 16) {
+      const int m = kv_gramh_mode();
+      return (m == 2 || (m == 1 && eval == GPB_KERNEL_RBF)) ? KV_GRAMH : KV_GRAM;
+    }
     if (T == 1 && !kv_gram1_disabled()) return KV_GRAM1;
   }
   if (T == 16 && DP % 4 == 0 && DP <= 32 && !kv_tc_disabled()) return KV_TC;

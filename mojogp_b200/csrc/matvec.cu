@@ -419,13 +419,13 @@ int launch_pack_gramh(const float* xs, int DP, float* v, int64_t v_ld, int c0, i
   return GPB_OK;
 }
 
-bool kv_gramh_disabled() {
+int kv_gramh_mode() {
   static int v = -1;
   if (v < 0) {
     const char* e = getenv("GPB_KV_GRAMH");
-    v = (e && e[0] == '0') ? 1 : 0;
+    v = (e && (e[0] == '0' || e[0] == '2')) ? e[0] - '0' : 1;
   }
-  return v == 1;
+  return v;
 }
 
 bool kv_gram1_disabled() {

@@ -61,7 +61,7 @@ def test_config3_row_sample_vs_oracle(gpb_lib):
     sq = _sqnorm(X, ell, "rbf")
     assert 50.0 < sq.max() < 100.0  # the operating point (57.9 at seed 3)
     prov = Provider(X, k, p, 0.0025)
-    assert prov.matvec_layout(t) == "gram-tensor-core"
+    assert prov.matvec_layout(t).startswith("gram-tensor-core")
     V = np.random.default_rng(7).standard_normal((t, n)).astype(np.float32)  # [t][n]
     vd = DeviceBuffer.from_host(np.ascontiguousarray(V))
     od = DeviceBuffer((t, n))
@@ -101,7 +101,7 @@ def test_near_gate_matvec_vs_oracle(gpb_lib, kname):
     k = make_ard_kernel(CTOR[kname](ard=True), d)
     p = _params(k, d, ell, rng)
     prov = Provider(X, k, p, 0.01)
-    assert prov.matvec_layout(t) == "gram-tensor-core"
+    assert prov.matvec_layout(t).startswith("gram-tensor-core")
     V = rng.standard_normal((X.shape[0], t)).astype(np.float32)
     ref = ok.forward_matvec(k.to_spec(d), p, X, V, noise=0.01)
     err = rel_fro(prov.matvec_host(V), ref)
@@ -115,7 +115,7 @@ def test_near_gate_matvec_vs_oracle(gpb_lib, kname):
 def _check_bilinear(X, k, p, d, rng):
     n, t = X.shape[0], 16
     prov = Provider(X, k, p, 0.01)
-    assert prov.matvec_layout(16) == "gram-tensor-core"
+    assert prov.matvec_layout(16).startswith("gram-tensor-core")
     A = rng.standard_normal((n, t)).astype(np.float32)
     B = rng.standard_normal((n, t)).astype(np.float32)
     ad = DeviceBuffer.from_host(np.ascontiguousarray(A.T))
@@ -161,7 +161,7 @@ def test_gb_kernel_config3_full_columns(gpb_lib):
     k = make_ard_kernel(RBF(ard=True), d)
     p = np.concatenate([ell, [1.0]]).astype(np.float32)
     prov = Provider(X, k, p, 0.0025)
-    assert prov.matvec_layout(16) == "gram-tensor-core"
+    assert prov.matvec_layout(16).startswith("gram-tensor-core")
     A = np.zeros((t, n), np.float32)
     A[:, rows] = rng.standard_normal((t, len(rows))).astype(np.float32)
     B = rng.standard_normal((t, n)).astype(np.float32)

@@ -78,7 +78,7 @@ def test_two_gpu_sharded_engine_matches_one_gpu(gpb_lib, tmp_path):
     # to that bar (the shards split the column range differently, so the
     # summation orders differ).
     for part in one["c3"] + two["c3"]:
-        assert part["c3_layout"] == "gram-tensor-core"
+        assert part["c3_layout"].startswith("gram-tensor-core")
         assert part["c3_err"] < 1e-5, part["c3_err"]
     def rows(parts):
         return {r: v for p in parts for r, v in zip(p["c3_rows"], p["c3_vals"])}
