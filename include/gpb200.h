@@ -98,6 +98,12 @@ int gpb_device_free(int32_t device, void* ptr);
 int gpb_memcpy_h2d(int32_t device, void* dst_dev, const void* src_host, int64_t bytes);
 int gpb_memcpy_d2h(int32_t device, void* dst_host, const void* src_dev, int64_t bytes);
 int gpb_memset_d(int32_t device, void* dst_dev, int32_t value, int64_t bytes);
+/* Page-lock (pin) / unpin an existing host buffer (cudaHostRegister /
+ * cudaHostUnregister) so copies to and from it run at full PCIe/C2C rate and
+ * stay asynchronous; no reference counterpart (the reference's host arrays
+ * are NumPy-owned and pageable). */
+int gpb_host_register(void* host_ptr, int64_t bytes);
+int gpb_host_unregister(void* host_ptr);
 
 /* ---------------------------------------------------------------- provider
  * Replaces init_provider() (fn_ptr_module.py:998-1115): copies X to the

@@ -30,6 +30,8 @@ SIGNATURES = {
     "gpb_device_free": [c_i32, P],
     "gpb_memcpy_h2d": [c_i32, P, P, c_i64],
     "gpb_memcpy_d2h": [c_i32, P, P, c_i64],
+    "gpb_host_register": [P, c_i64],
+    "gpb_host_unregister": [P],
     "gpb_memset_d": [c_i32, P, c_i32, c_i64],
     "gpb_provider_create": [P, c_i64, c_i32, P, c_i32, P, c_i32, c_f32, P, c_i32, PP],
     "gpb_provider_destroy": [P],

@@ -433,6 +433,18 @@ int gpb_memcpy_d2h(int32_t device, void* dst_host, const void* src_dev, int64_t 
   return GPB_OK;
 }
 
+int gpb_host_register(void* host_ptr, int64_t bytes) {
+  GPB_REQUIRE(host_ptr && bytes > 0, GPB_ERR_INVALID, "bad host buffer");
+  GPB_CHECK_CUDA(cudaHostRegister(host_ptr, (size_t)bytes, cudaHostRegisterPortable));
+  return GPB_OK;
+}
+
+int gpb_host_unregister(void* host_ptr) {
+  GPB_REQUIRE(host_ptr, GPB_ERR_INVALID, "null host buffer");
+  GPB_CHECK_CUDA(cudaHostUnregister(host_ptr));
+  return GPB_OK;
+}
+
 int gpb_memset_d(int32_t device, void* dst_dev, int32_t value, int64_t bytes) {
   GPB_REQUIRE(bytes >= 0 && (bytes == 0 || dst_dev), GPB_ERR_INVALID, "bad memset");
   GPB_CHECK_CUDA(cudaSetDevice(device));

@@ -47,8 +47,11 @@ class DeviceBuffer:
             raise ValueError(f"size mismatch: {a.nbytes} vs {self.nbytes} bytes")
         _lib.call("gpb_memcpy_h2d", self.device, C.c_void_p(self.ptr), _ptr(a), self.nbytes)
 
-    def download(self) -> np.ndarray:
-        out = np.empty(self.shape, dtype=self.dtype)
+    def download(self, out: np.ndarray | None = None) -> np.ndarray:
+        if out is None:
+            out = np.empty(self.shape, dtype=self.dtype)
+        elif out.nbytes != self.nbytes or not out.flags.c_contiguous or out.dtype != self.dtype:
+            raise ValueError("out must be a C-contiguous array of the buffer's size and dtype")
         _lib.call("gpb_memcpy_d2h", self.device, _ptr(out), C.c_void_p(self.ptr), self.nbytes)
         return out
 
@@ -248,3 +251,27 @@ def destroy_provider(info: dict) -> None:
     prov = info.get("provider")
     if prov is not None:
         prov.destroy()
+
+
+class pinned:
+    """Page-lock the given C-contiguous host arrays for the duration of a
+    ``with`` block (gpb_host_register / gpb_host_unregister), so copies to and
+    from them are DMA transfers from pinned memory."""
+
+    def __init__(self, *arrays: np.ndarray):
+        for a in arrays:
+            if not a.flags.c_contiguous:
+                raise ValueError("pinned arrays must be C-contiguous")
+        self.arrays = [a for a in arrays if a.nbytes > 0]
+        self._done: list[np.ndarray] = []
+
+    def __enter__(self):
+        for a in self.arrays:
+            _lib.call("gpb_host_register", _ptr(a), a.nbytes)
+            self._done.append(a)
+        return self
+
+    def __exit__(self, *exc):
+        while self._done:
+            _lib.call("gpb_host_unregister", _ptr(self._done.pop()))
+        return False

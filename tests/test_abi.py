@@ -69,3 +69,10 @@ def test_spec_encoding_layout():
     assert spec[2] == 4  # leaf, leaf, scale, sum
     rt = KernelNode.from_dict(k.to_dict())
     assert np.array_equal(rt.to_spec(3), spec)
+
+
+def test_host_register_rejects_bad_buffers(gpb_lib):
+    assert _lib.lib().gpb_host_register(None, 16) == _lib.ERR_INVALID
+    a = np.zeros(4, np.float32)
+    assert _lib.lib().gpb_host_register(C.c_void_p(a.ctypes.data), 0) == _lib.ERR_INVALID
+    assert _lib.lib().gpb_host_unregister(None) == _lib.ERR_INVALID
