@@ -184,3 +184,30 @@ def test_gradient_matvec_reference_layout(gpb_lib):
     prov.gradient_matvec(od1, vd, t, 1)
     prov.synchronize()
     assert rel_fro(od1.download().T, G[1] @ V) < 1e-5
+
+
+def test_host_matvec_from_pinned_buffers(gpb_lib):
+    """gpb_forward_matvec_host reads and writes page-locked host buffers
+    (gpb_host_register) with the same result as pageable ones, and the
+    buffers stay usable after unregistering."""
+    import ctypes as C
+
+    from mojogp_b200 import _lib
+    from mojogp_b200.provider import pinned
+
+    rng = np.random.default_rng(31)
+    n, d, t = 3000, 16, 16
+    X = rng.standard_normal((n, d)).astype(np.float32)
+    k = make_ard_kernel(RBF(ard=True), d)
+    p = rng.uniform(0.8, 3.0, size=d + 1).astype(np.float32)
+    prov = Provider(X, k, p, 0.01)
+    Vc = np.ascontiguousarray(rng.standard_normal((t, n)).astype(np.float32))
+    ref = prov.matvec_host(Vc.T)
+    out = np.empty_like(Vc)
+    with pinned(Vc, out):
+        for _ in range(2):
+            out[:] = 0
+            _lib.call("gpb_forward_matvec_host", prov.h, C.c_void_p(out.ctypes.data),
+                      C.c_void_p(Vc.ctypes.data), t)
+            assert rel_fro(out.T, ref) < 1e-6
+    assert rel_fro(out.T, ok.forward_matvec(k.to_spec(d), p, X, Vc.T, noise=0.01)) < 1e-5
